@@ -1,0 +1,229 @@
+"""ctypes view of the CPU oracle (svkv_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: the checker for the CUDA library.  Only tests/,
+__graft_entry__.smoke() and bench.py's CPU-baseline / reference arm import this
+module; the product path (skyvision.cpp_b200/) never does.
+
+Each function names the reference behaviour it restates; the C file carries the
+file:line citations.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsvkv_oracle.so")
+
+TYPE_F32, TYPE_F16, TYPE_Q8_0 = 0, 1, 8
+QK8_0, Q8_0_BYTES = 32, 34
+MASK_NONE, MASK_CAUSAL, MASK_WINDOW, MASK_EXPLICIT = 0, 1, 2, 3
+
+_lib = None
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc, OpenMP)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(
+                os.path.join(HERE, "svkv_oracle.c")):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P, I64, I32, F32, U64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_uint64
+        L.orc_f32_to_f16.restype = ctypes.c_uint16
+        L.orc_f32_to_f16.argtypes = [F32]
+        L.orc_f16_to_f32.restype = F32
+        L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.orc_f32_to_f16_n.argtypes = [P, P, I64]
+        L.orc_f16_to_f32_n.argtypes = [P, P, I64]
+        L.orc_normal_f16.argtypes = [U64, U64, U64, I64, F32, ctypes.c_double, F32, P]
+        L.orc_stream_base.restype = U64
+        L.orc_stream_base.argtypes = [U64, U64]
+        L.orc_q8_0_row.argtypes = [P, I64, P]
+        L.orc_q8_0_dequant_row.argtypes = [P, I64, P]
+        L.orc_set_rows.restype = I32
+        L.orc_set_rows.argtypes = [P, I32, I64, I64, ctypes.c_size_t, P, I32, ctypes.c_size_t, I64, P, I64]
+        L.orc_attn.restype = I32
+        L.orc_attn.argtypes = [P, I64, I32, I32, I32, P, P, I32, ctypes.c_size_t, I32, I32,
+                               I32, I32, P, P, P, P, I64, F32, P]
+        L.orc_soft_max_row.argtypes = [P, P, I32, F32, P]
+        L.orc_can_splice.restype = I32
+        L.orc_can_splice.argtypes = [P, I64, I64, P, I64]
+        L.orc_evict_window.argtypes = [P, P, P, I32, P, P]
+        L.orc_compact_rows.restype = I32
+        L.orc_compact_rows.argtypes = [P, ctypes.c_size_t, I64, P, I64, I64]
+        L.orc_num_threads.restype = I32
+        L.orc_set_num_threads.argtypes = [I32]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def num_threads() -> int:
+    return lib().orc_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    lib().orc_set_num_threads(int(n))
+
+
+# ----------------------------------------------------------------- numbers
+def f32_to_f16(x) -> np.ndarray:
+    """f32 -> f16 bits, round-to-nearest-even (ggml_fp32_to_fp16)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().orc_f32_to_f16_n(_p(x), _p(out), x.size)
+    return out
+
+
+def f16_to_f32(h) -> np.ndarray:
+    h = np.ascontiguousarray(h).view(np.uint16)
+    out = np.empty(h.shape, dtype=np.float32)
+    lib().orc_f16_to_f32_n(_p(h), _p(out), h.size)
+    return out
+
+
+def normal_f16(seed: int, stream: int, n: int, scale: float = 1.0, offset: int = 0,
+               outlier_frac: float = 0.0, outlier_mul: float = 8.0) -> np.ndarray:
+    """Seeded synthetic values: splitmix64 counter stream + Box-Muller, f16 bits.
+
+    The reference names no generator for the BASELINE configs; this one is the
+    documented stand-in (config 4 adds 1% outliers x8)."""
+    out = np.empty(int(n), dtype=np.uint16)
+    lib().orc_normal_f16(seed, stream, offset, int(n), scale, outlier_frac, outlier_mul, _p(out))
+    return out
+
+
+# ----------------------------------------------------------------- q8_0
+def row_bytes(type_: int, ne0: int) -> int:
+    if type_ == TYPE_F32:
+        return 4 * ne0
+    if type_ == TYPE_F16:
+        return 2 * ne0
+    if type_ == TYPE_Q8_0:
+        return ne0 // QK8_0 * Q8_0_BYTES
+    raise ValueError(type_)
+
+
+def q8_0_quantize(x) -> np.ndarray:
+    """x f32 [..., ne0] -> ggml block_q8_0 bytes [..., ne0/32*34]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    ne0 = x.shape[-1]
+    rows = x.reshape(-1, ne0)
+    out = np.empty((rows.shape[0], row_bytes(TYPE_Q8_0, ne0)), dtype=np.uint8)
+    L = lib()
+    for i in range(rows.shape[0]):
+        L.orc_q8_0_row(_p(rows[i]), ne0, _p(out[i]))
+    return out.reshape(x.shape[:-1] + (out.shape[-1],))
+
+
+def q8_0_dequant(b, ne0: int) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    rows = b.reshape(-1, b.shape[-1])
+    out = np.empty((rows.shape[0], ne0), dtype=np.float32)
+    L = lib()
+    for i in range(rows.shape[0]):
+        L.orc_q8_0_dequant_row(_p(rows[i]), ne0, _p(out[i]))
+    return out.reshape(b.shape[:-1] + (ne0,))
+
+
+def dequant_rows(cache: np.ndarray, type_: int, ne0: int) -> np.ndarray:
+    """cache bytes [rows, row_bytes] -> f32 [rows, ne0]."""
+    if type_ == TYPE_F16:
+        return f16_to_f32(np.ascontiguousarray(cache).view(np.uint16).reshape(cache.shape[0], ne0))
+    if type_ == TYPE_F32:
+        return np.ascontiguousarray(cache).view(np.float32).reshape(cache.shape[0], ne0).copy()
+    return q8_0_dequant(cache, ne0)
+
+
+# ----------------------------------------------------------------- set_rows
+def set_rows(dst: np.ndarray, dst_type: int, ne0: int, src: np.ndarray, src_type: int,
+             rows=None, base: int = 0) -> int:
+    """ggml_set_rows into dst (uint8 [dst_rows, row_bytes], modified in place).
+
+    src: uint8/f16/f32 rows [n_rows, ...] packed; rows None = cpy-into-view at base."""
+    dst_rows = dst.shape[0]
+    src = np.ascontiguousarray(src)
+    n_rows = src.shape[0]
+    src_nb1 = src.nbytes // max(n_rows, 1)
+    r = None if rows is None else np.ascontiguousarray(rows, dtype=np.int32)
+    return lib().orc_set_rows(_p(dst), dst_type, ne0, dst_rows, dst.strides[0],
+                              _p(src), src_type, src_nb1, n_rows, _p(r), base)
+
+
+# ----------------------------------------------------------------- attention
+def attn(q: np.ndarray, k: np.ndarray, v: np.ndarray, kv_type: int, n_kv_head: int, head_dim: int,
+         n_keys: int, scale: float, mask_mode: int = MASK_CAUSAL, causal_base: int = 0,
+         lo=None, hi=None, own=None, mask=None) -> np.ndarray:
+    """ggml_flash_attn_ext over a cache view.
+
+    q f32 [T, NH, HD]; k/v cache bytes [rows >= n_keys, row_bytes] (token-major
+    [NKV*HD] rows, ggml's [NKV*HD, n_ctx] tensor); returns f32 [T, NH, HD]."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    T, NH, HD = q.shape
+    assert HD == head_dim
+    k = np.ascontiguousarray(k)
+    v = np.ascontiguousarray(v)
+    assert k.strides[0] == v.strides[0]
+    out = np.empty((T, NH, HD), dtype=np.float32)
+    lo_ = None if lo is None else np.ascontiguousarray(lo, dtype=np.int32)
+    hi_ = None if hi is None else np.ascontiguousarray(hi, dtype=np.int32)
+    own_ = None if own is None else np.ascontiguousarray(own, dtype=np.int32)
+    m = None if mask is None else np.ascontiguousarray(mask).view(np.uint16)
+    m_nb1 = 0 if m is None else m.shape[-1]
+    rc = lib().orc_attn(_p(q), NH * HD, T, NH, HD, _p(k), _p(v), kv_type, k.strides[0],
+                        n_kv_head, n_keys, mask_mode, causal_base, _p(lo_), _p(hi_), _p(own_),
+                        _p(m), m_nb1, scale, _p(out))
+    if rc != 0:
+        raise ValueError(f"orc_attn failed: {rc}")
+    return out
+
+
+def soft_max_row(x, mask=None, scale: float = 1.0) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty_like(x)
+    m = None if mask is None else np.ascontiguousarray(mask).view(np.uint16)
+    lib().orc_soft_max_row(_p(x), _p(m), x.size, scale, _p(y))
+    return y
+
+
+# ----------------------------------------------------------------- session logic
+def can_splice(cached_ids, n_past: int, ids) -> bool:
+    c = np.ascontiguousarray(cached_ids, dtype=np.int32)
+    i = np.ascontiguousarray(ids, dtype=np.int32)
+    return bool(lib().orc_can_splice(_p(c), c.size, n_past, _p(i), i.size))
+
+
+def evict_window(turn_frames, n_marks: int, max_frames: int):
+    """qwen3vl window rule -> (kept turn frames, n_marks, drop_turns, drop_frames)."""
+    tf = np.ascontiguousarray(turn_frames, dtype=np.int32).copy()
+    nt = ctypes.c_int(tf.size)
+    nm = ctypes.c_int(n_marks)
+    dt = ctypes.c_int(0)
+    df = ctypes.c_int(0)
+    lib().orc_evict_window(_p(tf) if tf.size else None, ctypes.byref(nt), ctypes.byref(nm), max_frames,
+                           ctypes.byref(dt), ctypes.byref(df))
+    return tf[: nt.value].copy(), nm.value, dt.value, df.value
+
+
+def compact_rows(cache: np.ndarray, keep, dst_base: int) -> None:
+    """Order-preserving in-place move of kept rows to dst_base.. (moss_vl kv_shift_rows)."""
+    k = np.ascontiguousarray(keep, dtype=np.int32)
+    rc = lib().orc_compact_rows(_p(cache), cache.strides[0], cache.shape[0], _p(k), k.size, dst_base)
+    if rc != 0:
+        raise ValueError("invalid kept-row list")
