@@ -1,0 +1,227 @@
+/*
+ * svkv.h - C ABI of the B200 (sm_100a) text-decoder KV-cache library.
+ *
+ * Drop-in for the per-layer ggml ops SkyVision.cpp's decoders emit on the KV
+ * path (reference paths relative to the SkyVision.cpp checkout):
+ *
+ *   ggml_set_rows(kv.k[il], k2, pos_slot)      src/core/blocks/llm_block.hpp:227-233,
+ *                                              src/models/qwen3vl/qwen3vl_model.cpp:652-655
+ *   ggml_cpy(src, ggml_view(cache, base..))    src/core/engine/stage_buf.hpp:53-56 (view sink form)
+ *   ggml_flash_attn_ext(qf, kf, vf, mask, ..)  llm_block.hpp:239-277, qwen3vl_model.cpp:657-663
+ *   mul_mat / soft_max_ext / mul_mat           src/models/gemma4/gemma4_model.cpp:683-692
+ *   vqa::KvCache alloc/clear/free              src/core/engine/attention.hpp:19-56
+ *   set_causal_mask / set_window_mask          attention.hpp:60-83 (in-kernel predicates here)
+ *   KV splice predicate                        qwen3vl_model.cpp:1165-1171
+ *   window eviction + in-place compaction      qwen3vl_model.cpp:1110-1124, moss_vl_model.cpp:264-291
+ *
+ * Conventions
+ *   - Every function returns an int status: SV_OK (0) or a negative SV_ERR_*.
+ *     No exception crosses this boundary.
+ *   - Device pointers are plain pointers into the device the handle lives on;
+ *     `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Calls are asynchronous on that stream unless documented otherwise.
+ *   - Nothing on the per-token path allocates: workspaces are reserved when a
+ *     handle is created (or passed in by the caller for the raw ggml-op forms).
+ *   - A handle is not thread-safe (vqa::Model is single-threaded per instance,
+ *     src/core/vqa.hpp:121-123); distinct handles are independent.
+ *   - Type ids are ggml's: F32 = 0, F16 = 1, Q8_0 = 8.
+ *   - Layout is ggml's: a cache tensor is [n_kv_head*head_dim, n_ctx], i.e.
+ *     token-major rows of n_kv_head*head_dim elements (q8_0: blocks of 32
+ *     int8 + one f16 scale, 34 bytes per block).
+ */
+#ifndef SVKV_H
+#define SVKV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define SV_OK 0
+#define SV_ERR_INVALID (-1)      /* bad argument (null handle, bad shape, ...) */
+#define SV_ERR_UNSUPPORTED (-2)  /* shape/type combination this build does not implement */
+#define SV_ERR_CUDA (-3)         /* a CUDA runtime/driver call failed */
+#define SV_ERR_NOMEM (-4)        /* device allocation failed (KvCache::alloc returning false) */
+#define SV_ERR_OVERFLOW (-5)     /* context overflow: rows beyond n_ctx (qwen3vl_model.cpp:719) */
+#define SV_ERR_WORKSPACE (-6)    /* caller workspace too small */
+#define SV_ERR_DEVICE (-7)       /* a kernel reported an error bit (see sv_kv_error) */
+
+#define SV_TYPE_F32 0
+#define SV_TYPE_F16 1
+#define SV_TYPE_Q8_0 8
+
+/* mask modes of the attention entry points */
+#define SV_MASK_NONE 0      /* every key of the view is visible */
+#define SV_MASK_CAUSAL 1    /* key s visible to query t iff s <= base + t (set_causal_mask) */
+#define SV_MASK_WINDOW 2    /* s in [lo[t], hi[t]) or s == own[t] (set_window_mask) */
+#define SV_MASK_EXPLICIT 3  /* additive f16 mask [S, T] (ggml's mask argument) */
+
+/* device error bits reported by sv_kv_error / the err_flag word */
+#define SV_DEVERR_ROW_RANGE 1   /* a set_rows target row was out of range; that row was skipped */
+#define SV_DEVERR_TIMEOUT 2     /* a bounded on-device wait expired; the kernel unwound */
+#define SV_DEVERR_SEGMENT 4     /* a compaction segment pointed outside the cache */
+
+/* Human-readable name of a status code. */
+const char* sv_status_string(int status);
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int sv_version(void);
+
+/* ================================================================ KV store
+ * Replaces vqa::KvCache (src/core/engine/attention.hpp:19-56): n_layer pairs
+ * of [n_kv_head*head_dim, n_ctx] K/V tensors in one device buffer, zero-filled
+ * at creation.  kv_type is SV_TYPE_F16 (the reference's only cache type) or
+ * SV_TYPE_Q8_0 (head_dim a multiple of 32).  The handle also owns the attention
+ * workspace (split-K partials) and a device error word.
+ */
+typedef struct sv_kv sv_kv;
+
+/* KvCache::alloc (attention.hpp:25-46).  Prints "kv cache: %.2f GB" to stderr
+ * like the reference.  SV_ERR_NOMEM when the buffer cannot be allocated. */
+int sv_kv_create(int device, int n_layer, int n_kv_head, int head_dim, int n_ctx, int kv_type,
+                 sv_kv** out);
+/* KvCache::free (attention.hpp:52-55). */
+int sv_kv_destroy(sv_kv* kv);
+/* KvCache::clear (attention.hpp:48-50): zero every K/V tensor (async). */
+int sv_kv_clear(sv_kv* kv, void* stream);
+/* kv.k[layer] / kv.v[layer] (attention.hpp:21): device pointer and row bytes,
+ * for callers that build ggml-style views themselves. */
+int sv_kv_tensor(const sv_kv* kv, int layer, int is_v, void** data, size_t* row_bytes);
+/* Shape of the cache. Any output pointer may be NULL. */
+int sv_kv_info(const sv_kv* kv, int* n_layer, int* n_kv_head, int* head_dim, int* n_ctx, int* kv_type);
+/* Read and clear the device error word (synchronises `stream`).  *flags gets
+ * the SV_DEVERR_* bits raised since the last call. */
+int sv_kv_error(sv_kv* kv, int* flags, void* stream);
+
+/* ================================================================ append
+ * ggml_set_rows(dst, src, rows) (llm_block.hpp:232-233) and the
+ * ggml_cpy-into-view form (rows == NULL: row i goes to base + i).
+ *   dst   [ne0, dst_rows] of dst_type (F16, Q8_0 or F32), row stride dst_nb1 bytes
+ *   src   [ne0, n_rows]   of src_type (F16 or F32),        row stride src_nb1 bytes
+ *   rows  device int32 [n_rows] or NULL
+ * f16 -> f16 is a byte copy, f32 -> f16 rounds to nearest even, and any -> q8_0
+ * uses ggml's block_q8_0 rounding (d = amax/127 in f32, q = round-half-away(x/d),
+ * d stored as f16).  A row outside [0, dst_rows) is skipped and raises
+ * SV_DEVERR_ROW_RANGE in *err_flag (device int, may be NULL) -- ggml asserts there.
+ */
+int sv_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
+                const void* src, int src_type, size_t src_nb1, int64_t n_rows,
+                const int32_t* rows, int64_t base, int* err_flag, void* stream);
+
+/* Both set_rows of one decoder layer in one launch
+ * (ggml_set_rows(kv.k[il], k2, pos_slot) + ggml_set_rows(kv.v[il], v2, pos_slot),
+ * qwen3vl_model.cpp:654-655).  k/v: device [n_rows][n_kv_head*head_dim] of
+ * src_type; rows: device int32 [n_rows] or NULL for base + i.
+ * SV_ERR_OVERFLOW when rows == NULL and base + n_rows > n_ctx. */
+int sv_kv_append(sv_kv* kv, int layer, const void* k, const void* v, int src_type, int n_rows,
+                 const int32_t* rows, int base, void* stream);
+
+/* ================================================================ attention
+ * ggml_flash_attn_ext(q, k, v, mask, scale, max_bias = 0, softcap = 0)
+ * (llm_block.hpp:268-277) with the reference's views spelled out as ggml
+ * ne/nb arrays:
+ *   q   [HD, T, NH]   F32 or F16   (qf = view of q3 with nb1 and nb2 swapped)
+ *   k,v [HD, S, NKV]  F16 or Q8_0  (nb1 = cache row stride, nb2 = one head's bytes)
+ *   mask F16 [S, >=T] additive, row stride mask_nb1 bytes, or NULL
+ *   dst F32 [HD, NH, T] contiguous
+ * GQA maps query head h to kv head h / (NH/NKV).  A query row that sees no key
+ * gets zeros.  Only max_bias == 0 and logit_softcap == 0 are supported (the
+ * only values the reference passes).  The workspace holds split-K partials:
+ * size it with sv_flash_attn_ext_workspace; a smaller one gives fewer splits,
+ * ws_bytes == 0 runs unsplit.
+ */
+typedef struct sv_fa_params {
+    const void* q;    int q_type;  int64_t q_ne[3];  size_t q_nb[3];
+    const void* k;    int k_type;  int64_t k_ne[3];  size_t k_nb[3];
+    const void* v;    int v_type;  int64_t v_ne[3];  size_t v_nb[3];
+    const void* mask; int64_t mask_ne1;  size_t mask_nb1;
+    float scale;
+    float max_bias;
+    float logit_softcap;
+    float* dst;
+} sv_fa_params;
+
+size_t sv_flash_attn_ext_workspace(const sv_fa_params* p);
+int sv_flash_attn_ext(const sv_fa_params* p, void* workspace, size_t ws_bytes, void* stream);
+
+/* Cache-level attention for one decoder layer (the FA node of
+ * qwen3vl_model.cpp:657-663 with the causal mask of set_causal_mask(mask,
+ * n_past, T) computed in-kernel): query t (0 <= t < T) attends cache rows
+ * [0, n_past + t].  q: device [T][n_head][head_dim] of q_type (F16/F32);
+ * out: device f32 [T][n_head][head_dim].  Single-token decode (T = 1) runs the
+ * split-K flash-decode kernel; chunks with T > 16/(NH/NKV) queries run the
+ * chunked-prefill kernel. */
+int sv_attn(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, int n_past,
+            float scale, float* out, void* stream);
+
+/* Multi-session attention over one shared cache (vc3_batch.inc:145-172 with
+ * set_window_mask, attention.hpp:71-83): query i attends rows [lo[i], hi[i])
+ * plus row own[i].  lo/hi/own: device int32 [n_q]; max_span: an upper bound
+ * on max_i(hi[i] - lo[i]) (sizes the grid).  q/out as in sv_attn with T = n_q. */
+int sv_attn_window(sv_kv* kv, int layer, const void* q, int q_type, int n_q, int n_head,
+                   const int32_t* lo, const int32_t* hi, const int32_t* own, int max_span,
+                   float scale, float* out, void* stream);
+
+/* ggml_soft_max_ext(x, mask, scale, max_bias = 0) of the mul_mat fallback
+ * (gemma4_model.cpp:685-691): y[r] = softmax(x[r]*scale + mask[r % mask_rows]).
+ * x, y: f32 rows of ne0 (strides in bytes); mask: F16 rows or NULL. */
+int sv_soft_max_ext(const float* x, int64_t ne0, int64_t n_rows, size_t x_nb1, const void* mask,
+                    int64_t mask_rows, size_t mask_nb1, float scale, float* y, size_t y_nb1,
+                    void* stream);
+
+/* ================================================================ eviction
+ * In-HBM, order-preserving compaction of every layer's K and V
+ * (the row move of kv_shift_rows, moss_vl_model.cpp:264-291, driven by the
+ * qwen3vl window rule, qwen3vl_model.cpp:1110-1124).  The cache rows
+ * [0, n_rows_used) are described by consecutive segments {src, n_rows, keep};
+ * kept segments are packed, in order, starting at dst_base (the destination of
+ * each kept row is dst_base + exclusive prefix sum of kept lengths).  Rows
+ * only move towards the front.  *new_len = dst_base + total kept rows.
+ * The segment table is host memory (the host owns the turn table). */
+typedef struct sv_segment {
+    int32_t src;     /* first cache row of the segment */
+    int32_t n_rows;  /* rows in the segment */
+    int32_t keep;    /* nonzero: the segment survives */
+} sv_segment;
+
+int sv_kv_compact(sv_kv* kv, const sv_segment* segs, int n_segs, int dst_base, int* new_len,
+                  void* stream);
+
+/* ================================================================ session
+ * Host-side KV bookkeeping of a streaming session (Qwen3VL's s_kv_ids /
+ * s_turns / n_past, qwen3vl_model.cpp:167-181).  The frames of a turn occupy
+ * rows_per_frame cache rows each, followed by the turn's text rows and its
+ * answer rows; an optional sink prefix [0, sink_rows) is never evicted.
+ */
+typedef struct sv_session sv_session;
+
+/* The splice predicate (qwen3vl_model.cpp:1167-1169): 1 if the cache holds
+ * exactly `cached` (kv_len == n_past) and `ids` strictly extends it, else 0.
+ * *skip (may be NULL) gets kv_len when splicing. Pure host function. */
+int sv_can_splice(const int32_t* cached, int64_t kv_len, int64_t n_past, const int32_t* ids,
+                  int64_t n_ids, int64_t* skip);
+
+/* kv may be NULL: the session then only plans rows (no device work). */
+int sv_session_create(sv_kv* kv, int max_frames, int rows_per_frame, int sink_rows, sv_session** out);
+int sv_session_destroy(sv_session* s);
+/* session_reset (qwen3vl_model.cpp:1059-1064): forget turns and rows (no device work). */
+int sv_session_reset(sv_session* s);
+/* Start a turn that brings n_new_frames frames: applies the window rule to the
+ * completed turns plus the new frames and compacts the cache when rows leave.
+ * *first_row gets the cache row where the new turn's rows start (the new
+ * n_past); *kept_new_frames how many of the new frames survive the window. */
+int sv_session_begin_turn(sv_session* s, int n_new_frames, int* first_row, int* kept_new_frames,
+                          void* stream);
+/* Close the turn: frames actually written, and the text / answer rows that
+ * followed them. */
+int sv_session_end_turn(sv_session* s, int frames, int text_rows, int answer_rows);
+/* Current row count and the kept-row map: rows_out[i] = the original (never
+ * compacted) row id of cache row i, i < *n_rows (max_rows caps the copy). */
+int sv_session_rows(const sv_session* s, int* n_rows, int64_t* rows_out, int max_rows);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SVKV_H */

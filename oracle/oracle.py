@@ -221,6 +221,64 @@ def evict_window(turn_frames, n_marks: int, max_frames: int):
     return tf[: nt.value].copy(), nm.value, dt.value, df.value
 
 
+class SessionRows:
+    """Which cache rows a streaming session keeps, turn by turn.
+
+    Restates Qwen3VL::ask_session's window (qwen3vl_model.cpp:1110-1124,
+    likewise MageVL::session_evict, mage_model.cpp:1827-1841) on a KV row
+    layout: a pinned prefix of sink rows, then per completed turn its frames
+    (rows_per_frame rows each), its text rows and its answer rows.  Dropping a
+    turn drops all its rows; trimming a frame (the reference erases the oldest
+    mark and decrements the front turn's frame count, clamped at 0) drops that
+    frame's rows, or a not-yet-written frame of the new turn when the front
+    turn has none left.  Row ids are the order in which rows were first written.
+    """
+
+    def __init__(self, max_frames: int, rows_per_frame: int, sink_rows: int = 0):
+        self.max_frames = max_frames
+        self.rpf = rows_per_frame
+        self.sink = list(range(sink_rows))
+        self.next_id = sink_rows
+        self.turns = []          # dicts: frames (list of row-id lists), text, answer (row-id lists)
+        self.marks = 0           # s_marks.size()
+        self.pending_new = 0
+
+    def begin_turn(self, n_new: int) -> int:
+        self.marks += n_new
+        new_kept = n_new
+        while self.marks > self.max_frames and len(self.turns) > 1:
+            self.marks -= len(self.turns[0]["frames"])
+            del self.turns[0]
+        while self.marks > self.max_frames:
+            self.marks -= 1
+            if self.turns and len(self.turns[0]["frames"]) > 0:
+                del self.turns[0]["frames"][0]
+            else:
+                new_kept -= 1
+        self.pending_new = new_kept
+        return new_kept
+
+    def end_turn(self, frames: int, text: int, answer: int) -> None:
+        t = {"frames": [], "text": [], "answer": []}
+        for _ in range(frames):
+            t["frames"].append(list(range(self.next_id, self.next_id + self.rpf)))
+            self.next_id += self.rpf
+        t["text"] = list(range(self.next_id, self.next_id + text))
+        self.next_id += text
+        t["answer"] = list(range(self.next_id, self.next_id + answer))
+        self.next_id += answer
+        self.marks -= self.pending_new - min(frames, self.pending_new)
+        self.turns.append(t)
+
+    def rows(self) -> np.ndarray:
+        out = list(self.sink)
+        for t in self.turns:
+            for f in t["frames"]:
+                out += f
+            out += t["text"] + t["answer"]
+        return np.array(out, dtype=np.int64)
+
+
 def compact_rows(cache: np.ndarray, keep, dst_base: int) -> None:
     """Order-preserving in-place move of kept rows to dst_base.. (moss_vl kv_shift_rows)."""
     k = np.ascontiguousarray(keep, dtype=np.int32)

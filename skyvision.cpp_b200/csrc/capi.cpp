@@ -1,0 +1,502 @@
+// capi.cpp - the extern "C" boundary (include/svkv.h): argument checking,
+// KV-store ownership, tensor maps, and the choice of kernel / split plan.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "internal.hpp"
+
+using namespace svkv;
+
+namespace svkv {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode;
+}
+
+}  // namespace
+
+bool encode_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t dim0, uint64_t dim1,
+                    uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swz) {
+    auto enc = encoder();
+    if (!enc) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride1_bytes & 15)) return false;
+    const cuuint64_t dims[2] = {dim0, dim1};
+    const cuuint64_t strides[1] = {stride1_bytes};
+    const cuuint32_t box[2] = {box0, box1};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_tmap_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, const uint64_t dims_in[3],
+                    const uint64_t strides_bytes[2], const uint32_t box_in[3], CUtensorMapSwizzle swz) {
+    auto enc = encoder();
+    if (!enc) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (strides_bytes[0] & 15) || (strides_bytes[1] & 15)) return false;
+    const cuuint64_t dims[3] = {dims_in[0], dims_in[1], dims_in[2]};
+    const cuuint64_t strides[2] = {strides_bytes[0], strides_bytes[1]};
+    const cuuint32_t box[3] = {box_in[0], box_in[1], box_in[2]};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+namespace {
+
+constexpr size_t kDefaultWsBytes = 64ull << 20;   // split-K partials per handle
+constexpr int kMaxTickets = 1 << 16;
+
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) { ok = false; return; }
+        if (prev != dev && cudaSetDevice(dev) != cudaSuccess) ok = false;
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+int cuda_status(cudaError_t e) {
+    if (e == cudaSuccess) return SV_OK;
+    fprintf(stderr, "svkv: CUDA error %s\n", cudaGetErrorString(e));
+    return SV_ERR_CUDA;
+}
+
+// --------------------------------------------------------------- split plan
+struct Plan {
+    int qpt = 1, n_qtiles = 1, chunk = 64, n_splits = 1;
+};
+
+// span: keys one query tile may touch; ws_floats: capacity for partials
+Plan plan_decode(int T, int G, int NKV, int span, int head_dim, bool window, size_t ws_floats, int n_tickets,
+                 int target_ctas) {
+    Plan p;
+    const int BK = decode_block_keys();
+    p.qpt = window ? 1 : std::max(1, 16 / G);
+    p.n_qtiles = ceil_div(T, p.qpt);
+    const int base = NKV * p.n_qtiles;
+    span = std::max(span, 1);
+    int want = std::max(1, ceil_div(target_ctas, base));
+    auto set_splits = [&](int w) {
+        p.chunk = std::max(BK, ceil_div(ceil_div(span, w), BK) * BK);
+        p.n_splits = ceil_div(span, p.chunk);
+    };
+    set_splits(want);
+    const size_t per = decode_partial_floats(head_dim);
+    while (p.n_splits > 1 && ((size_t)base * p.n_splits * per > ws_floats || base > n_tickets)) {
+        want = std::max(1, want / 2);
+        set_splits(want);
+        if (want == 1) break;
+    }
+    if (p.n_splits > 1 && ((size_t)base * p.n_splits * per > ws_floats || base > n_tickets)) {
+        p.chunk = ceil_div(span, BK) * BK;
+        p.n_splits = 1;
+    }
+    return p;
+}
+
+int target_ctas_default() { return kNumSMs; }
+
+}  // namespace
+}  // namespace svkv
+
+// ===================================================================== C ABI
+extern "C" {
+
+const char* sv_status_string(int status) {
+    switch (status) {
+        case SV_OK: return "ok";
+        case SV_ERR_INVALID: return "invalid argument";
+        case SV_ERR_UNSUPPORTED: return "unsupported shape or type";
+        case SV_ERR_CUDA: return "CUDA error";
+        case SV_ERR_NOMEM: return "device allocation failed";
+        case SV_ERR_OVERFLOW: return "context overflow";
+        case SV_ERR_WORKSPACE: return "workspace too small";
+        case SV_ERR_DEVICE: return "device-side error flag raised";
+        default: return "unknown status";
+    }
+}
+
+int sv_version(void) { return 100; }
+
+int sv_kv_create(int device, int n_layer, int n_kv_head, int head_dim, int n_ctx, int kv_type, sv_kv** out) {
+    if (!out || n_layer <= 0 || n_kv_head <= 0 || head_dim <= 0 || n_ctx <= 0) return SV_ERR_INVALID;
+    if (kv_type != SV_TYPE_F16 && kv_type != SV_TYPE_Q8_0) return SV_ERR_UNSUPPORTED;
+    if (kv_type == SV_TYPE_Q8_0 && (head_dim % kQK8_0) != 0) return SV_ERR_UNSUPPORTED;
+    *out = nullptr;
+    DeviceGuard g(device);
+    if (!g.ok) return SV_ERR_CUDA;
+    sv_kv* kv = new sv_kv();
+    kv->device = device;
+    kv->n_layer = n_layer;
+    kv->n_kv_head = n_kv_head;
+    kv->head_dim = head_dim;
+    kv->n_ctx = n_ctx;
+    kv->type = kv_type;
+    kv->row_bytes = row_bytes_of(kv_type, (int64_t)n_kv_head * head_dim);
+    kv->tensor_bytes = (kv->row_bytes * (size_t)n_ctx + 255) / 256 * 256;
+    const size_t total = kv->tensor_bytes * 2 * (size_t)n_layer;
+    if (cudaMalloc(&kv->buf, total) != cudaSuccess) {
+        fprintf(stderr, "KV cache allocation failed (%.2f GB)\n", (double)total / 1e9);
+        cudaGetLastError();
+        delete kv;
+        return SV_ERR_NOMEM;
+    }
+    bool ok = cudaMemset(kv->buf, 0, total) == cudaSuccess;
+    kv->ws_bytes = kDefaultWsBytes;
+    kv->n_tickets = kMaxTickets;
+    ok = ok && cudaMalloc(&kv->ws, kv->ws_bytes) == cudaSuccess;
+    ok = ok && cudaMalloc(&kv->tickets, sizeof(int) * kv->n_tickets) == cudaSuccess;
+    ok = ok && cudaMemset(kv->tickets, 0, sizeof(int) * kv->n_tickets) == cudaSuccess;
+    ok = ok && cudaMalloc(&kv->err, sizeof(int)) == cudaSuccess;
+    ok = ok && cudaMemset(kv->err, 0, sizeof(int)) == cudaSuccess;
+    ok = ok && cudaMalloc(&kv->scratch, kv->tensor_bytes) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        sv_kv_destroy(kv);
+        return SV_ERR_NOMEM;
+    }
+    if (decode_supported(head_dim, kv_type, kv->row_bytes, n_kv_head)) {
+        kv->tm_dec.resize(2 * n_layer);
+        for (int i = 0; i < 2 * n_layer; i++)
+            if (!make_decode_tmap(&kv->tm_dec[i], kv->tensor(i / 2, i % 2), kv_type, head_dim, n_kv_head,
+                                  kv->row_bytes, n_ctx)) {
+                sv_kv_destroy(kv);
+                return SV_ERR_CUDA;
+            }
+    }
+    if (prefill_supported(head_dim, kv_type, 4, kv->row_bytes)) {
+        kv->tm_pre.resize(2 * n_layer);
+        for (int i = 0; i < 2 * n_layer; i++)
+            if (!make_prefill_tmap(&kv->tm_pre[i], kv->tensor(i / 2, i % 2), head_dim, n_kv_head, kv->row_bytes,
+                                   n_ctx)) {
+                sv_kv_destroy(kv);
+                return SV_ERR_CUDA;
+            }
+    }
+    fprintf(stderr, "kv cache: %.2f GB (n_ctx %d)\n", (double)total / 1e9, n_ctx);
+    *out = kv;
+    return SV_OK;
+}
+
+int sv_kv_destroy(sv_kv* kv) {
+    if (!kv) return SV_ERR_INVALID;
+    DeviceGuard g(kv->device);
+    if (kv->buf) cudaFree(kv->buf);
+    if (kv->ws) cudaFree(kv->ws);
+    if (kv->tickets) cudaFree(kv->tickets);
+    if (kv->err) cudaFree(kv->err);
+    if (kv->scratch) cudaFree(kv->scratch);
+    delete kv;
+    return SV_OK;
+}
+
+int sv_kv_clear(sv_kv* kv, void* stream) {
+    if (!kv) return SV_ERR_INVALID;
+    DeviceGuard g(kv->device);
+    return cuda_status(cudaMemsetAsync(kv->buf, 0, kv->tensor_bytes * 2 * (size_t)kv->n_layer,
+                                       static_cast<cudaStream_t>(stream)));
+}
+
+int sv_kv_tensor(const sv_kv* kv, int layer, int is_v, void** data, size_t* row_bytes) {
+    if (!kv || layer < 0 || layer >= kv->n_layer) return SV_ERR_INVALID;
+    if (data) *data = kv->tensor(layer, is_v ? 1 : 0);
+    if (row_bytes) *row_bytes = kv->row_bytes;
+    return SV_OK;
+}
+
+int sv_kv_info(const sv_kv* kv, int* n_layer, int* n_kv_head, int* head_dim, int* n_ctx, int* kv_type) {
+    if (!kv) return SV_ERR_INVALID;
+    if (n_layer) *n_layer = kv->n_layer;
+    if (n_kv_head) *n_kv_head = kv->n_kv_head;
+    if (head_dim) *head_dim = kv->head_dim;
+    if (n_ctx) *n_ctx = kv->n_ctx;
+    if (kv_type) *kv_type = kv->type;
+    return SV_OK;
+}
+
+int sv_kv_error(sv_kv* kv, int* flags, void* stream) {
+    if (!kv || !flags) return SV_ERR_INVALID;
+    DeviceGuard g(kv->device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, kv->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->err, 0, sizeof(int), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    *flags = h;
+    return cuda_status(e);
+}
+
+// ------------------------------------------------------------------ append
+int sv_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1, const void* src,
+                int src_type, size_t src_nb1, int64_t n_rows, const int32_t* rows, int64_t base, int* err_flag,
+                void* stream) {
+    if (!dst || (!src && n_rows > 0) || ne0 <= 0 || dst_rows <= 0 || n_rows < 0) return SV_ERR_INVALID;
+    if (dst_type != SV_TYPE_F16 && dst_type != SV_TYPE_Q8_0 && dst_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (src_type != SV_TYPE_F16 && src_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (dst_type == SV_TYPE_Q8_0 && ne0 % kQK8_0 != 0) return SV_ERR_UNSUPPORTED;
+    if (dst_type == SV_TYPE_F32 && src_type != SV_TYPE_F32 && src_type != SV_TYPE_F16) return SV_ERR_UNSUPPORTED;
+    if (dst_nb1 < row_bytes_of(dst_type, ne0) || src_nb1 < row_bytes_of(src_type, ne0)) return SV_ERR_INVALID;
+    if (!rows && (base < 0 || base + n_rows > dst_rows)) return SV_ERR_OVERFLOW;
+    return cuda_status(launch_set_rows(dst, dst_type, ne0, dst_rows, dst_nb1, src, src_type, src_nb1, n_rows, rows,
+                                       base, err_flag, 1, 0, 0, static_cast<cudaStream_t>(stream)));
+}
+
+int sv_kv_append(sv_kv* kv, int layer, const void* k, const void* v, int src_type, int n_rows, const int32_t* rows,
+                 int base, void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !k || !v || n_rows < 0) return SV_ERR_INVALID;
+    if (src_type != SV_TYPE_F16 && src_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (!rows && (base < 0 || base + n_rows > kv->n_ctx)) return SV_ERR_OVERFLOW;
+    if (n_rows == 0) return SV_OK;
+    DeviceGuard g(kv->device);
+    const int64_t ne0 = (int64_t)kv->n_kv_head * kv->head_dim;
+    const size_t src_nb1 = row_bytes_of(src_type, ne0);
+    // K and V in one launch: blockIdx.y selects the tensor; V sits one tensor after K
+    // in the cache buffer, and the V source is addressed relative to the K source.
+    const uint8_t* kb = static_cast<const uint8_t*>(k);
+    const uint8_t* vb = static_cast<const uint8_t*>(v);
+    if (vb > kb) {
+        return cuda_status(launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
+                                           src_nb1, n_rows, rows, base, kv->err, 2, kv->tensor_bytes,
+                                           (size_t)(vb - kb), static_cast<cudaStream_t>(stream)));
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
+                                    src_nb1, n_rows, rows, base, kv->err, 1, 0, 0, st);
+    if (e == cudaSuccess)
+        e = launch_set_rows(kv->tensor(layer, 1), kv->type, ne0, kv->n_ctx, kv->row_bytes, v, src_type, src_nb1,
+                            n_rows, rows, base, kv->err, 1, 0, 0, st);
+    return cuda_status(e);
+}
+
+// ------------------------------------------------------------------ attention
+static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* tv, const CUtensorMap* tkp,
+                         const CUtensorMap* tvp, int head_dim, int kv_type, AttnArgs& a, int span, bool window,
+                         float* ws, size_t ws_bytes, int* tickets, int n_tickets, cudaStream_t st) {
+    (void)kvh;
+    // chunked prefill on the tensor-core kernel when it applies
+    if (!window && tkp && tvp && a.mask_mode == SV_MASK_CAUSAL && a.T * a.G > 16) {
+        return cuda_status(launch_prefill(a, head_dim, tkp, tvp, st));
+    }
+    const size_t ws_floats = ws ? ws_bytes / sizeof(float) : 0;
+    Plan p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0,
+                         target_ctas_default());
+    a.qpt = p.qpt;
+    a.n_qtiles = p.n_qtiles;
+    a.chunk = p.chunk;
+    a.n_splits = p.n_splits;
+    if (a.n_splits > 1) {
+        const size_t n_part = (size_t)a.NKV * a.n_qtiles * a.n_splits * 16;
+        a.ws_o = ws;
+        a.ws_ml = ws + n_part * head_dim;
+        a.tickets = tickets;
+    }
+    return cuda_status(launch_decode(a, head_dim, kv_type, tk, tv, st));
+}
+
+int sv_attn(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, int n_past, float scale, float* out,
+            void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !q || !out || T <= 0 || n_head <= 0 || n_past < 0)
+        return SV_ERR_INVALID;
+    if (q_type != SV_TYPE_F16 && q_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (n_head % kv->n_kv_head != 0 || n_head / kv->n_kv_head > 16) return SV_ERR_UNSUPPORTED;
+    if (n_past + T > kv->n_ctx) return SV_ERR_OVERFLOW;
+    if (kv->tm_dec.empty()) return SV_ERR_UNSUPPORTED;
+    DeviceGuard g(kv->device);
+    const int HD = kv->head_dim;
+    const int es = q_type == SV_TYPE_F32 ? 4 : 2;
+    AttnArgs a{};
+    a.q = static_cast<const uint8_t*>(q);
+    a.q_type = q_type;
+    a.q_nb_h = (int64_t)HD * es;
+    a.q_nb_t = (int64_t)n_head * HD * es;
+    a.T = T;
+    a.NH = n_head;
+    a.NKV = kv->n_kv_head;
+    a.G = n_head / kv->n_kv_head;
+    a.S = n_past + T;
+    a.row_base = 0;
+    a.mask_mode = SV_MASK_CAUSAL;
+    a.causal_base = n_past;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.out = out;
+    a.out_nb_h = HD;
+    a.out_nb_t = (int64_t)n_head * HD;
+    a.err = kv->err;
+    const CUtensorMap* tkp = kv->tm_pre.empty() ? nullptr : &kv->tm_pre[2 * layer];
+    const CUtensorMap* tvp = kv->tm_pre.empty() ? nullptr : &kv->tm_pre[2 * layer + 1];
+    return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], tkp, tvp, HD, kv->type, a,
+                         n_past + T, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int sv_attn_window(sv_kv* kv, int layer, const void* q, int q_type, int n_q, int n_head, const int32_t* lo,
+                   const int32_t* hi, const int32_t* own, int max_span, float scale, float* out, void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !q || !out || n_q <= 0 || n_head <= 0 || !lo || !hi || !own ||
+        max_span < 0)
+        return SV_ERR_INVALID;
+    if (q_type != SV_TYPE_F16 && q_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (n_head % kv->n_kv_head != 0 || n_head / kv->n_kv_head > 16) return SV_ERR_UNSUPPORTED;
+    if (kv->tm_dec.empty()) return SV_ERR_UNSUPPORTED;
+    DeviceGuard g(kv->device);
+    const int HD = kv->head_dim;
+    const int es = q_type == SV_TYPE_F32 ? 4 : 2;
+    AttnArgs a{};
+    a.q = static_cast<const uint8_t*>(q);
+    a.q_type = q_type;
+    a.q_nb_h = (int64_t)HD * es;
+    a.q_nb_t = (int64_t)n_head * HD * es;
+    a.T = n_q;
+    a.NH = n_head;
+    a.NKV = kv->n_kv_head;
+    a.G = n_head / kv->n_kv_head;
+    a.S = kv->n_ctx;
+    a.mask_mode = SV_MASK_WINDOW;
+    a.lo = lo;
+    a.hi = hi;
+    a.own = own;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.out = out;
+    a.out_nb_h = HD;
+    a.out_nb_t = (int64_t)n_head * HD;
+    a.err = kv->err;
+    return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], nullptr, nullptr, HD, kv->type, a,
+                         max_span + 1, true, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
+                         static_cast<cudaStream_t>(stream));
+}
+
+// ggml_flash_attn_ext with explicit views
+static int check_fa(const sv_fa_params* p, int* HD, int* T, int* NH, int* S, int* NKV) {
+    if (!p || !p->q || !p->k || !p->v || !p->dst) return SV_ERR_INVALID;
+    if (p->max_bias != 0.0f || p->logit_softcap != 0.0f) return SV_ERR_UNSUPPORTED;
+    if (p->q_type != SV_TYPE_F16 && p->q_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (p->k_type != p->v_type || (p->k_type != SV_TYPE_F16 && p->k_type != SV_TYPE_Q8_0)) return SV_ERR_UNSUPPORTED;
+    *HD = (int)p->q_ne[0];
+    *T = (int)p->q_ne[1];
+    *NH = (int)p->q_ne[2];
+    *S = (int)p->k_ne[1];
+    *NKV = (int)p->k_ne[2];
+    if (p->k_ne[0] != *HD || p->v_ne[0] != *HD || p->v_ne[1] != *S || p->v_ne[2] != *NKV) return SV_ERR_INVALID;
+    if (*T <= 0 || *NH <= 0 || *S <= 0 || *NKV <= 0 || *NH % *NKV != 0 || *NH / *NKV > 16) return SV_ERR_UNSUPPORTED;
+    const size_t headb = row_bytes_of(p->k_type, *HD);
+    // the kernel addresses a head as a column offset inside one cache row: heads packed in the row
+    if (p->k_nb[2] != headb || p->v_nb[2] != headb || p->k_nb[1] != p->v_nb[1]) return SV_ERR_UNSUPPORTED;
+    if (p->mask && p->mask_ne1 < *T) return SV_ERR_INVALID;
+    return SV_OK;
+}
+
+size_t sv_flash_attn_ext_workspace(const sv_fa_params* p) {
+    int HD, T, NH, S, NKV;
+    if (check_fa(p, &HD, &T, &NH, &S, &NKV) != SV_OK) return 0;
+    Plan pl = plan_decode(T, NH / NKV, NKV, S, HD, false, (size_t)1 << 40, kMaxTickets, target_ctas_default());
+    if (pl.n_splits <= 1) return 0;
+    const size_t tiles = (size_t)NKV * pl.n_qtiles;
+    return tiles * pl.n_splits * decode_partial_floats(HD) * sizeof(float) + tiles * sizeof(int) + 256;
+}
+
+int sv_flash_attn_ext(const sv_fa_params* p, void* workspace, size_t ws_bytes, void* stream) {
+    int HD, T, NH, S, NKV;
+    int rc = check_fa(p, &HD, &T, &NH, &S, &NKV);
+    if (rc != SV_OK) return rc;
+    const size_t row_stride = p->k_nb[1];
+    if (!decode_supported(HD, p->k_type, row_stride, NKV)) return SV_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(p->k) & 15) || (reinterpret_cast<uintptr_t>(p->v) & 15)) return SV_ERR_UNSUPPORTED;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the views' K/V base is where key 0 of kv head 0 starts; rows are row_stride apart
+    CUtensorMap tk, tv;
+    if (!make_decode_tmap(&tk, p->k, p->k_type, HD, NKV, row_stride, S) ||
+        !make_decode_tmap(&tv, p->v, p->v_type, HD, NKV, row_stride, S))
+        return SV_ERR_UNSUPPORTED;
+    const int es = p->q_type == SV_TYPE_F32 ? 4 : 2;
+    if (p->q_nb[0] != (size_t)es) return SV_ERR_UNSUPPORTED;
+    AttnArgs a{};
+    a.q = static_cast<const uint8_t*>(p->q);
+    a.q_type = p->q_type;
+    a.q_nb_t = (int64_t)p->q_nb[1];
+    a.q_nb_h = (int64_t)p->q_nb[2];
+    a.T = T;
+    a.NH = NH;
+    a.NKV = NKV;
+    a.G = NH / NKV;
+    a.S = S;
+    a.mask_mode = p->mask ? SV_MASK_EXPLICIT : SV_MASK_NONE;
+    a.mask = static_cast<const uint16_t*>(p->mask);
+    a.mask_nb_t = (int64_t)(p->mask_nb1 / 2);
+    a.mask_rows = (int)p->mask_ne1;
+    a.scale_log2 = p->scale * 1.4426950408889634f;
+    a.out = p->dst;
+    a.out_nb_h = HD;
+    a.out_nb_t = (int64_t)NH * HD;
+    a.err = nullptr;
+    // workspace: [partials][tickets]; tickets are zeroed here so any caller buffer works
+    float* ws = nullptr;
+    int* tickets = nullptr;
+    size_t wsb = 0;
+    int n_tk = 0;
+    if (workspace && ws_bytes > 1024) {
+        Plan pl = plan_decode(T, a.G, NKV, S, HD, false, (size_t)1 << 40, kMaxTickets, target_ctas_default());
+        const size_t tiles = (size_t)NKV * pl.n_qtiles;
+        const size_t tk_bytes = (tiles * sizeof(int) + 255) / 256 * 256;
+        if (ws_bytes > tk_bytes + 256) {
+            tickets = static_cast<int*>(workspace);
+            n_tk = (int)tiles;
+            ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + tk_bytes);
+            wsb = ws_bytes - tk_bytes;
+            cudaError_t e = cudaMemsetAsync(tickets, 0, tiles * sizeof(int), st);
+            if (e != cudaSuccess) return cuda_status(e);
+        }
+    }
+    return run_attention(nullptr, &tk, &tv, nullptr, nullptr, HD, p->k_type, a, S, false, ws, wsb, tickets, n_tk, st);
+}
+
+int sv_soft_max_ext(const float* x, int64_t ne0, int64_t n_rows, size_t x_nb1, const void* mask, int64_t mask_rows,
+                    size_t mask_nb1, float scale, float* y, size_t y_nb1, void* stream) {
+    if (!x || !y || ne0 <= 0 || n_rows < 0 || (mask && mask_rows <= 0)) return SV_ERR_INVALID;
+    if (n_rows == 0) return SV_OK;
+    return cuda_status(launch_soft_max(x, ne0, n_rows, x_nb1, static_cast<const uint16_t*>(mask), mask_rows, mask_nb1,
+                                       scale, y, y_nb1, static_cast<cudaStream_t>(stream)));
+}
+
+// ------------------------------------------------------------------ eviction
+int sv_kv_compact(sv_kv* kv, const sv_segment* segs, int n_segs, int dst_base, int* new_len, void* stream) {
+    if (!kv || (!segs && n_segs > 0) || n_segs < 0 || dst_base < 0) return SV_ERR_INVALID;
+    if (n_segs > 1024) return SV_ERR_UNSUPPORTED;
+    int64_t kept = 0;
+    int64_t prev_end = -1;
+    for (int s = 0; s < n_segs; s++) {
+        if (segs[s].n_rows < 0 || segs[s].src < 0 || (int64_t)segs[s].src + segs[s].n_rows > kv->n_ctx)
+            return SV_ERR_INVALID;
+        if (segs[s].src < prev_end) return SV_ERR_INVALID;       // segments ascend and do not overlap
+        prev_end = (int64_t)segs[s].src + segs[s].n_rows;
+        if (segs[s].keep) {
+            if (segs[s].n_rows > 0 && (int64_t)segs[s].src < dst_base + kept) return SV_ERR_INVALID;   // front only
+            kept += segs[s].n_rows;
+        }
+    }
+    if (new_len) *new_len = (int)(dst_base + kept);
+    DeviceGuard g(kv->device);
+    return cuda_status(launch_compact(kv, nullptr, segs, n_segs, dst_base, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

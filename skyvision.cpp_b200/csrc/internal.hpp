@@ -1,0 +1,119 @@
+// internal.hpp - library-internal types shared by the .cu/.cpp files.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/svkv.h"
+
+namespace svkv {
+
+constexpr int kQK8_0 = 32;
+constexpr int kQ8_0Bytes = 34;
+constexpr int kNumSMs = 148;
+
+inline size_t row_bytes_of(int type, int64_t ne0) {
+    switch (type) {
+        case SV_TYPE_F32: return (size_t)ne0 * 4;
+        case SV_TYPE_F16: return (size_t)ne0 * 2;
+        case SV_TYPE_Q8_0: return (size_t)(ne0 / kQK8_0) * kQ8_0Bytes;
+        default: return 0;
+    }
+}
+
+inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// ------------------------------------------------------------ attention args
+// One attention launch: queries x one kv view.  All strides in bytes.
+struct AttnArgs {
+    const uint8_t* q;       // query element (t, h, e) at q + t*q_nb_t + h*q_nb_h + e*q_es
+    int64_t q_nb_t, q_nb_h;
+    int q_type;             // SV_TYPE_F16 / SV_TYPE_F32
+    int T, NH, NKV, G;      // G = NH / NKV
+    int qpt;                // queries per 16-row tile (decode kernel)
+    int n_qtiles;
+    int S;                  // keys in the view
+    int row_base;           // tensor row of view key 0 (TMA y coordinate offset)
+    int mask_mode;
+    int causal_base;
+    const int32_t* lo;      // window mode, device [T]
+    const int32_t* hi;
+    const int32_t* own;
+    const uint16_t* mask;   // explicit mode: f16 row t at mask + t*mask_nb_t (elements)
+    int64_t mask_nb_t;
+    int mask_rows;          // rows available in the mask (query t uses row t)
+    float scale_log2;       // scale * log2(e)
+    int chunk;              // keys per split
+    int n_splits;
+    float* out;             // (t, h, e) at out + t*out_nb_t + h*out_nb_h + e (floats)
+    int64_t out_nb_t, out_nb_h;
+    float* ws_o;            // split partials [tile][split][16][HD]
+    float* ws_ml;           // [tile][split][16][2]
+    int* tickets;           // [tile], zero between launches
+    int* err;
+};
+
+struct PrefillArgs;  // attn_prefill.cu
+
+// ------------------------------------------------------------ handle
+struct KvHandle {
+    int device = 0;
+    int n_layer = 0, n_kv_head = 0, head_dim = 0, n_ctx = 0, type = SV_TYPE_F16;
+    size_t row_bytes = 0, tensor_bytes = 0;
+    uint8_t* buf = nullptr;              // 2*n_layer tensors, K then V per layer
+    std::vector<CUtensorMap> tm_dec;     // decode-box tensor maps: [2*layer + is_v]
+    std::vector<CUtensorMap> tm_pre;     // prefill-box tensor maps (f16 caches), same indexing
+    float* ws = nullptr;                 // split-K partials
+    size_t ws_bytes = 0;
+    int* tickets = nullptr;
+    int n_tickets = 0;
+    int* err = nullptr;                  // device error word
+    uint8_t* scratch = nullptr;          // one tensor's worth of rows for compaction fallback
+
+    uint8_t* tensor(int layer, int is_v) const {
+        return buf + (size_t)(2 * layer + is_v) * tensor_bytes;
+    }
+};
+
+// ------------------------------------------------------------ host helpers
+bool encode_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t dim0,
+                    uint64_t dim1, uint64_t stride1_bytes, uint32_t box0, uint32_t box1,
+                    CUtensorMapSwizzle swz);
+bool encode_tmap_3d(CUtensorMap* m, const void* base, CUtensorMapDataType dt, const uint64_t dims[3],
+                    const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swz);
+
+// decode kernel: can this (head_dim, kv type, row layout) run?
+bool decode_supported(int head_dim, int kv_type, size_t row_bytes, int n_kv_head);
+// build the decode tensor map of one cache view tensor
+bool make_decode_tmap(CUtensorMap* m, const void* base, int kv_type, int head_dim, int n_kv_head,
+                      size_t row_bytes, int64_t n_rows);
+size_t decode_partial_floats(int head_dim);   // floats per (tile, split) partial incl. m/l
+int decode_block_keys();                       // BK
+cudaError_t launch_decode(const AttnArgs& a, int head_dim, int kv_type, const CUtensorMap* tk,
+                          const CUtensorMap* tv, cudaStream_t st);
+
+// prefill (tcgen05) kernel
+bool prefill_supported(int head_dim, int kv_type, int G, size_t row_bytes);
+bool make_prefill_tmap(CUtensorMap* m, const void* base, int head_dim, int n_kv_head, size_t row_bytes,
+                       int64_t n_rows);
+cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
+                           cudaStream_t st);
+
+cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
+                            const void* src, int src_type, size_t src_nb1, int64_t n_rows,
+                            const int32_t* rows, int64_t base, int* err, int n_tensors,
+                            size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st);
+
+cudaError_t launch_compact(KvHandle* kv, const int32_t* seg_dev_unused, const sv_segment* segs, int n_segs,
+                           int dst_base, cudaStream_t st);
+
+cudaError_t launch_soft_max(const float* x, int64_t ne0, int64_t n_rows, size_t x_nb1, const uint16_t* mask,
+                            int64_t mask_rows, size_t mask_nb1, float scale, float* y, size_t y_nb1,
+                            cudaStream_t st);
+
+}  // namespace svkv
+
+struct sv_kv : svkv::KvHandle {};

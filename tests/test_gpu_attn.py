@@ -1,0 +1,232 @@
+"""GQA attention over the cache on the GPU against the oracle.
+
+Tolerance (the north-star gate): max-abs <= 2e-3 and relative L2 <= 1e-3
+against the fp32-accumulated CPU result.  Cases: the reference's own test
+geometries (nemotron scenario_attn, minicpmo FA probe and KV-cached steps,
+through the golden fixtures), the BASELINE geometries (32q/8kv HD128 f16;
+16q/4kv HD256 q8_0 with outliers), decode at block edges, short chunks,
+explicit masks, per-session windows, and the soft_max fallback op.
+"""
+import numpy as np
+import pytest
+import torch
+
+from __graft_entry__ import load_package
+
+sv = load_package()
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+MAX_ABS, REL_L2 = 2e-3, 1e-3
+
+
+def close(got, ref, max_abs=MAX_ABS, rel=REL_L2):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.abs(got - ref)
+    r = np.linalg.norm(got - ref) / max(np.linalg.norm(ref), 1e-30)
+    assert np.isfinite(got).all()
+    assert d.max() <= max_abs and r <= rel, (float(d.max()), float(r))
+
+
+def fill_cache(orc, kv, layer, n_rows, seed, outliers=0.0):
+    """Append n_rows seeded f16 K/V rows at base 0; returns the f16 source bits."""
+    ne0 = kv.n_kv_head * kv.head_dim
+    k = orc.normal_f16(seed, 100 + layer, n_rows * ne0, outlier_frac=outliers).reshape(n_rows, ne0)
+    v = orc.normal_f16(seed, 200 + layer, n_rows * ne0, outlier_frac=outliers).reshape(n_rows, ne0)
+    kv.append(layer, torch.from_numpy(k.view(np.float16)).to(DEV), torch.from_numpy(v.view(np.float16)).to(DEV),
+              base=0)
+    return k, v
+
+
+def ref_attn(orc, kv, layer, q_bits, n_past, scale):
+    kc = kv.tensor(layer, 0).cpu().numpy()
+    vc = kv.tensor(layer, 1).cpu().numpy()
+    T = q_bits.shape[0]
+    return orc.attn(orc.f16_to_f32(q_bits), kc, vc, kv.kv_type, kv.n_kv_head, kv.head_dim, n_past + T, scale,
+                    orc.MASK_CAUSAL, n_past)
+
+
+# ------------------------------------------------------------------ reference test geometries
+def test_golden_nemotron_scenario(golden):
+    """nemotronomni_seg_test scenario_attn: 8q/2kv HD16, cache 16, prefill 6 then decode at 6, 7, 8."""
+    NH, NKV, HD, S = 8, 2, 16, 16
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, NKV, HD, S)
+    k = torch.from_numpy(golden["nemo_k"].view(np.float16).reshape(9, NKV * HD)).to(DEV)
+    v = torch.from_numpy(golden["nemo_v"].view(np.float16).reshape(9, NKV * HD)).to(DEV)
+    q = torch.from_numpy(golden["nemo_q"]).to(DEV)                    # f32 queries like ggml's q3
+    kv.append(0, k[:6], v[:6], rows=torch.arange(6, dtype=torch.int32, device=DEV))
+    out = kv.attn(0, q[:6].contiguous(), n_past=0, scale=1 / np.sqrt(HD))
+    close(out.cpu().numpy(), golden["nemo_prefill_out"])
+    for s in range(3):
+        p = 6 + s
+        kv.append(0, k[p:p + 1], v[p:p + 1], rows=torch.tensor([p], dtype=torch.int32, device=DEV))
+        out = kv.attn(0, q[p:p + 1].contiguous(), n_past=p, scale=1 / np.sqrt(HD))
+        close(out.cpu().numpy()[0], golden["nemo_decode_out"][s])
+    assert np.array_equal(kv.tensor(0, 0).cpu().numpy().view(np.uint16).reshape(S, NKV, HD), golden["nemo_final_kcache"])
+    assert np.array_equal(kv.tensor(0, 1).cpu().numpy().view(np.uint16).reshape(S, NKV, HD), golden["nemo_final_vcache"])
+
+
+def test_golden_minicpmo_probe(golden):
+    """minicpmo_seg_test scenario_fa_probe (F16 KV): 16 queries, 40 keys, 8 heads, dh 32, no mask."""
+    q = torch.from_numpy(golden["probe_q"]).to(DEV)
+    k = torch.from_numpy(golden["probe_k"].view(np.uint8)).to(DEV)
+    v = torch.from_numpy(golden["probe_v"].view(np.uint8)).to(DEV)
+    out = sv.flash_attn_ext(q, k, v, None, 1 / np.sqrt(32), n_kv_head=8, head_dim=32, n_keys=40)
+    close(out.cpu().numpy(), golden["probe_out"])
+
+
+def test_golden_minicpmo_kv_steps(golden):
+    NH, NKV, HD = 8, 2, 16
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, NKV, HD, 32)
+    n_past = 0
+    for i in range(3):
+        q = torch.from_numpy(golden[f"cpmo_q{i}"]).to(DEV)
+        k = torch.from_numpy(golden[f"cpmo_k{i}"].view(np.float16).reshape(-1, NKV * HD)).to(DEV)
+        v = torch.from_numpy(golden[f"cpmo_v{i}"].view(np.float16).reshape(-1, NKV * HD)).to(DEV)
+        T = q.shape[0]
+        kv.append(0, k, v, base=n_past)
+        out = kv.attn(0, q, n_past=n_past, scale=1 / np.sqrt(HD))
+        close(out.cpu().numpy(), golden[f"cpmo_out{i}"])
+        n_past += T
+
+
+def test_golden_baseline_geometry(golden):
+    q = torch.from_numpy(golden["geo_q"]).to(DEV)
+    k = torch.from_numpy(golden["geo_k"].view(np.float16).reshape(80, -1)).to(DEV)
+    v = torch.from_numpy(golden["geo_v"].view(np.float16).reshape(80, -1)).to(DEV)
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, 8, 128, 128)
+    kv.append(0, k, v, base=0)
+    out = kv.attn(0, q, n_past=int(golden["geo_base"]), scale=1 / np.sqrt(128))
+    close(out.cpu().numpy(), golden["geo_out"])
+
+
+# ------------------------------------------------------------------ decode sweeps
+@pytest.mark.parametrize("n_past", [0, 1, 63, 64, 65, 255, 1023, 1024, 1087, 4095])
+def test_decode_cfg1_geometry(orc, n_past):
+    """BASELINE config 1 geometry: 32q/8kv HD128 f16 cache of 4096, one query at n_past."""
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, 8, 128, 4096)
+    fill_cache(orc, kv, 0, n_past + 1, seed=0)
+    q = orc.normal_f16(0, 9 + n_past, 32 * 128).reshape(1, 32, 128)
+    out = kv.attn(0, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / np.sqrt(128))
+    close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n_past, 1 / np.sqrt(128)))
+
+
+@pytest.mark.parametrize("T,n_past", [(2, 100), (3, 1000), (4, 4091), (7, 50), (16, 300), (33, 17)])
+def test_short_chunks(orc, T, n_past):
+    kv = sv.KvCache()
+    assert kv.alloc(0, 2, 8, 128, 4096)
+    fill_cache(orc, kv, 1, n_past + T, seed=1)
+    q = orc.normal_f16(1, 50 + T, T * 32 * 128).reshape(T, 32, 128)
+    out = kv.attn(1, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / np.sqrt(128))
+    close(out.cpu().numpy(), ref_attn(orc, kv, 1, q, n_past, 1 / np.sqrt(128)))
+
+
+@pytest.mark.parametrize("hd,nkv,nh", [(64, 4, 16), (256, 4, 16), (128, 8, 8), (128, 2, 32), (32, 8, 8), (16, 2, 8)])
+def test_decode_head_geometries(orc, hd, nkv, nh):
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, nkv, hd, 2048)
+    n_past = 1500
+    fill_cache(orc, kv, 0, n_past + 1, seed=2)
+    q = orc.normal_f16(2, hd + nh, nh * hd).reshape(1, nh, hd)
+    out = kv.attn(0, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / np.sqrt(hd))
+    close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n_past, 1 / np.sqrt(hd)))
+
+
+def test_decode_f32_query(orc):
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, 8, 128, 1024)
+    fill_cache(orc, kv, 0, 700, seed=3)
+    q16 = orc.normal_f16(3, 77, 32 * 128).reshape(1, 32, 128)
+    q = orc.f16_to_f32(q16)                     # f32 activations that are f16-exact
+    out = kv.attn(0, torch.from_numpy(q).to(DEV), n_past=699, scale=1 / np.sqrt(128))
+    close(out.cpu().numpy(), ref_attn(orc, kv, 0, q16, 699, 1 / np.sqrt(128)))
+
+
+# ------------------------------------------------------------------ q8_0 cache (config 4)
+@pytest.mark.parametrize("n_past,T", [(0, 1), (511, 1), (2000, 1), (777, 3)])
+def test_decode_q8_0_outliers(orc, n_past, T):
+    """16q/4kv HD256 q8_0 cache, K/V f16 N(0,1) with 1% outliers x8."""
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, 4, 256, 4096, sv.TYPE_Q8_0)
+    fill_cache(orc, kv, 0, n_past + T, seed=3, outliers=0.01)
+    q = orc.normal_f16(3, 300 + n_past, T * 16 * 256).reshape(T, 16, 256)
+    out = kv.attn(0, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / 16.0)
+    close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n_past, 1 / 16.0))
+
+
+# ------------------------------------------------------------------ explicit mask / ggml view form
+def test_flash_attn_ext_explicit_mask(orc):
+    """ggml_flash_attn_ext with a host-built set_causal_mask-style f16 mask plus random holes."""
+    NKV, HD, NH, S, T, base = 8, 128, 32, 600, 4, 590
+    ne0 = NKV * HD
+    k = orc.normal_f16(4, 1, S * ne0).reshape(S, ne0)
+    v = orc.normal_f16(4, 2, S * ne0).reshape(S, ne0)
+    q = orc.normal_f16(4, 3, T * NH * HD).reshape(T, NH, HD)
+    rng = np.random.default_rng(4)
+    mask = np.zeros((T, S), np.float32)
+    for t in range(T):
+        mask[t, base + t + 1:] = -np.inf
+    mask[rng.random((T, S)) < 0.1] = -np.inf
+    mask[:, :5] += rng.standard_normal((T, 5)).astype(np.float32)     # additive values, not just 0/-inf
+    m16 = mask.astype(np.float16)
+    kd = torch.from_numpy(k.view(np.uint8).reshape(S, -1)).to(DEV)
+    vd = torch.from_numpy(v.view(np.uint8).reshape(S, -1)).to(DEV)
+    out = sv.flash_attn_ext(torch.from_numpy(q.view(np.float16)).to(DEV), kd, vd, torch.from_numpy(m16).to(DEV),
+                            1 / np.sqrt(HD), NKV, HD, S)
+    ref = orc.attn(orc.f16_to_f32(q), k.view(np.uint8).reshape(S, -1), v.view(np.uint8).reshape(S, -1),
+                   orc.TYPE_F16, NKV, HD, S, 1 / np.sqrt(HD), orc.MASK_EXPLICIT, mask=m16.view(np.uint16))
+    close(out.cpu().numpy(), ref)
+
+
+def test_fully_masked_row_is_zero(orc):
+    NKV, HD, NH, S = 2, 64, 8, 70
+    k = orc.normal_f16(5, 1, S * NKV * HD).reshape(S, -1)
+    q = orc.normal_f16(5, 2, 2 * NH * HD).reshape(2, NH, HD)
+    m16 = np.zeros((2, S), np.float16)
+    m16[0, :] = -np.inf
+    kd = torch.from_numpy(k.view(np.uint8).reshape(S, -1)).to(DEV)
+    out = sv.flash_attn_ext(torch.from_numpy(q.view(np.float16)).to(DEV), kd, kd, torch.from_numpy(m16).to(DEV),
+                            0.125, NKV, HD, S).cpu().numpy()
+    assert np.all(out[0] == 0)
+    assert np.isfinite(out[1]).all() and np.abs(out[1]).max() > 0
+
+
+# ------------------------------------------------------------------ multi-session windows
+def test_window_multi_session(orc):
+    """vc3_batch-style decode: sessions in slot ranges of one cache, set_window_mask per query."""
+    NKV, HD, NH = 8, 128, 32
+    lens = [1, 63, 64, 500, 2047, 1300, 7, 3000]
+    cap_each = 3072
+    n = len(lens)
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, NKV, HD, cap_each * n)
+    fill_cache(orc, kv, 0, cap_each * n, seed=6)
+    lo = np.array([i * cap_each for i in range(n)], np.int32)
+    hi = lo + np.array(lens, np.int32) + 1                    # the query's own new row included
+    own = hi - 1
+    q = orc.normal_f16(6, 9, n * NH * HD).reshape(n, NH, HD)
+    td = lambda a: torch.from_numpy(a).to(DEV)
+    out = kv.attn_window(0, td(q.view(np.float16)), td(lo), td(hi), td(own), int((hi - lo).max()), 1 / np.sqrt(HD))
+    kc = kv.tensor(0, 0).cpu().numpy()
+    vc = kv.tensor(0, 1).cpu().numpy()
+    ref = orc.attn(orc.f16_to_f32(q), kc, vc, orc.TYPE_F16, NKV, HD, cap_each * n, 1 / np.sqrt(HD), orc.MASK_WINDOW,
+                   lo=lo, hi=hi, own=own)
+    close(out.cpu().numpy(), ref)
+
+
+# ------------------------------------------------------------------ soft_max fallback
+@pytest.mark.parametrize("ne0,rows", [(1088, 32), (33, 5), (4096, 3)])
+def test_soft_max_ext(orc, ne0, rows):
+    rng = np.random.default_rng(ne0)
+    x = (rng.standard_normal((rows, ne0)) * 3).astype(np.float32)
+    mask = np.zeros((2, ne0), np.float16)
+    mask[0, ne0 // 2:] = -np.inf
+    mask[1, :3] = 1.5
+    got = sv.soft_max_ext(torch.from_numpy(x).to(DEV), torch.from_numpy(mask).to(DEV), scale=0.3).cpu().numpy()
+    for r in range(rows):
+        ref = orc.soft_max_row(x[r], mask[r % 2].view(np.uint16), scale=0.3)
+        np.testing.assert_allclose(got[r], ref, rtol=1e-5, atol=1e-7)
