@@ -1,0 +1,490 @@
+#!/usr/bin/env python3
+"""Benchmark of the KV-cache hot path (BASELINE metric: decode attention tokens/s,
+KV GB/s against HBM, prefill attention TFLOP/s; 1..8 GPUs).
+
+Workload (the metric's configuration that fits one GPU):
+the Qwen3-VL-4B text geometry -- 36 layers, 32 query / 8 KV heads, head_dim 128,
+f16 KV cache of 8192 rows.  Turn 1 fills 4096 rows per layer (untimed); turn
+2's prompt strictly extends turn 1, so the splice predicate holds and only the
+384-token tail is chunk-prefilled against the 4096 cached rows (timed
+separately -> prefill TFLOP/s); then decode steps run.  One *step* is one
+decode token through all 36 layers: per layer the K/V append of the new row
+and the causal GQA attention over the whole cache.  With the default
+--steps 128 the timed steps are exactly config 2's 128 decode steps
+(S = 4481 .. 4608).  Inputs are synthetic N(0,1) f16 from a seeded torch CUDA
+generator (seed 1); every decode step reads ~670 MB of K/V, larger than the
+126 MB L2, so no flush is needed between steps.
+
+On N GPUs (torchrun, one rank per GPU) every rank serves its own independent
+session (sessions shard across GPUs; no collective on the data path), so
+scaling is weak and value = N * steps / max-over-ranks time.
+
+--impl reference times the CPU implementation of the same path on the host
+cores (the C restatement of the reference's ggml CPU semantics in oracle/;
+the reference's ggml is not vendored and cannot be built here) for the same
+metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L, NH, NKV, HD, CAP = 36, 32, 8, 128, 8192
+PRE, TAIL, DEC = 4096, 384, 128
+SEED = 1
+SCALE = 1.0 / np.sqrt(HD)
+METRIC = "decode attn tokens/s & KV GB/s vs 8 TB/s; prefill attn TFLOP/s; 1/2/4/8 GPU"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=DEC)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="svkv", choices=["svkv", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes from a committed ncu summary (profiles/<name>.md), if present."""
+    path = os.path.join(ROOT, "profiles", name + ".md")
+    try:
+        for line in open(path):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def decode_attn_bytes(S: int) -> int:
+    """Algorithmic bytes of one decode-attention launch: K and V rows of every kv head + Q + O."""
+    return S * NKV * HD * 2 * 2 + NH * HD * 2 + NH * HD * 4
+
+
+def append_bytes(n_rows: int) -> int:
+    return n_rows * NKV * HD * 2 * 2 * 2      # read K+V source, write K+V cache
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """NVML SM clock + throttle reasons sampled in a thread during the timed region."""
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.stop_ev = threading.Event()
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.h = None
+            uuid = getattr(torch.cuda.get_device_properties(device_index), "uuid", None)
+            if uuid is not None:
+                try:
+                    self.h = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}")
+                except Exception:
+                    self.h = None
+            if self.h is None:
+                cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+                ids = [c for c in cvd.split(",") if c.strip().isdigit()]
+                idx = int(ids[device_index]) if device_index < len(ids) else device_index
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.nv = pynvml
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop_ev.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                rs = self.reasons_fn(self.h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self.stop_ev.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        nv = self.nv
+        names = {
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        seen = set()
+        for _, rs in self.samples:
+            for n, bit in names.items():
+                if rs & bit:
+                    seen.add(n)
+        mhz = [m for m, _ in self.samples]
+        return {"sm_mhz": float(np.median(mhz)), "sm_max_mhz": self.max_mhz, "reasons": sorted(seen),
+                "samples": len(mhz)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------ CPU path (oracle restatement)
+def cpu_decode_sample(n_layers: int, n_tokens: int, seed: int = SEED):
+    """Decode tokens through n_layers of the config-2 geometry on the host (the oracle's
+    set_rows + flash-attention restatement, all OpenMP threads).  Returns seconds per
+    token-layer and the thread count."""
+    from oracle import oracle as orc
+    ne0 = NKV * HD
+    n_rows = PRE + TAIL + n_tokens
+    caches = []
+    for layer in range(n_layers):
+        k = np.zeros((CAP, ne0 * 2), np.uint8)
+        v = np.zeros((CAP, ne0 * 2), np.uint8)
+        k[:PRE + TAIL] = orc.normal_f16(seed, 10 + layer, (PRE + TAIL) * ne0).view(np.uint8).reshape(PRE + TAIL, -1)
+        v[:PRE + TAIL] = orc.normal_f16(seed, 90 + layer, (PRE + TAIL) * ne0).view(np.uint8).reshape(PRE + TAIL, -1)
+        caches.append((k, v))
+    qs = [orc.f16_to_f32(orc.normal_f16(seed, 500 + i, NH * HD)).reshape(1, NH, HD) for i in range(n_tokens)]
+    ks = [orc.normal_f16(seed, 700 + i, ne0).reshape(1, ne0) for i in range(n_tokens)]
+    t0 = time.perf_counter()
+    for i in range(n_tokens):
+        n_past = PRE + TAIL + i
+        for layer in range(n_layers):
+            k, v = caches[layer]
+            orc.set_rows(k, orc.TYPE_F16, ne0, ks[i], orc.TYPE_F16, base=n_past)
+            orc.set_rows(v, orc.TYPE_F16, ne0, ks[i], orc.TYPE_F16, base=n_past)
+            orc.attn(qs[i], k, v, orc.TYPE_F16, NKV, HD, n_past + 1, SCALE, orc.MASK_CAUSAL, n_past)
+    dt = time.perf_counter() - t0
+    assert n_rows <= CAP
+    return dt / (n_tokens * n_layers), orc.num_threads()
+
+
+def run_reference(args, world, rank):
+    """The reference arm: the CPU path, same metric, rank 0 only."""
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+    orc.build()
+    sample_layers = 4
+    # warm-up, then K timed steps; each step = one decode token through a sample of layers
+    cpu_decode_sample(sample_layers, max(1, args.warmup))
+    per_tl_all, cores = cpu_decode_sample(sample_layers, args.steps)
+    step_s = per_tl_all * L                       # one token through all 36 layers
+    value = 1.0 / step_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "BASELINE config 2 decode (36 layers, 32q/8kv, HD 128, f16 KV, S 4481..4608)",
+                   "sessions_per_gpu": 1},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} decode tokens through {sample_layers} of 36 layers, "
+                                   f"per-token time scaled x{L / sample_layers:g}"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU path
+def run_svkv(args, world, rank, local):
+    import torch
+    from __graft_entry__ import load_package
+    sv = load_package()
+    dev = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED * 1000 + rank)
+    K, W = args.steps, args.warmup
+    if PRE + TAIL + max(K, W) > CAP:
+        raise SystemExit(f"steps beyond the {CAP}-row cache")
+
+    kv = sv.KvCache()
+    if not kv.alloc(local, L, NKV, HD, CAP):
+        raise SystemExit("KvCache.alloc failed")
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).to(torch.float16)
+
+    ne0 = NKV * HD
+    launches = 0
+    with torch.cuda.stream(stream):
+        # ---- turn 1: 4096 rows per layer
+        for layer in range(L):
+            kv.append(layer, randn(PRE, ne0), randn(PRE, ne0), base=0, stream=stream)
+        ids1 = np.arange(PRE, dtype=np.int32) % 151000
+        ids2 = np.concatenate([ids1, (np.arange(TAIL, dtype=np.int32) * 7) % 151000])
+        skip = sv.can_splice(ids1, PRE, ids2)          # turn 2 strictly extends turn 1
+        assert skip == PRE
+
+        # ---- turn 2 tail: chunked prefill of 384 rows against the 4096 cached
+        tq = [randn(TAIL, NH, HD) for _ in range(L)]
+        tk = [randn(TAIL, ne0) for _ in range(L)]
+        tv = [randn(TAIL, ne0) for _ in range(L)]
+        tout = torch.empty(TAIL, NH, HD, dtype=torch.float32, device=dev)
+
+        def tail_pass():
+            for layer in range(L):
+                kv.append(layer, tk[layer], tv[layer], base=skip, stream=stream)
+                kv.attn(layer, tq[layer], n_past=skip, scale=SCALE, out=tout, stream=stream)
+
+        tail_pass()
+        stream.synchronize()
+        reps = 3
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            tail_pass()
+        e1.record(stream)
+        e1.synchronize()
+        prefill_ms = e0.elapsed_time(e1) / reps
+        vis = TAIL * skip + TAIL * (TAIL + 1) // 2
+        prefill_flop = 4.0 * NH * HD * vis * L
+        prefill_tflops = prefill_flop / (prefill_ms * 1e-3) / 1e12
+
+        # ---- decode: one CUDA graph per step, replayed; n_past lives on the device
+        n0 = PRE + TAIL
+        max_keys = n0 + max(K, W) + 1
+        npast = torch.full((1,), n0, dtype=torch.int32, device=dev)
+        dq = randn(L, 1, NH, HD)
+        dk = randn(L, 1, ne0)
+        dvv = randn(L, 1, ne0)
+        dout = torch.empty(L, 1, NH, HD, dtype=torch.float32, device=dev)
+
+        def step():
+            for layer in range(L):
+                kv.append_at(layer, dk[layer], dvv[layer], npast, stream=stream)
+                kv.attn_at(layer, dq[layer], npast, max_keys, SCALE, out=dout[layer], stream=stream)
+            sv.counter_add(npast, 1, stream=stream)
+
+        step()                                     # eager run before capture (sets kernel attributes)
+        stream.synchronize()
+        npast.fill_(n0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        stream.synchronize()
+        for _ in range(W):
+            g.replay()
+        stream.synchronize()
+        npast.fill_(n0)
+        # clock settle (untimed) so the sampled clocks reflect steady load
+        for _ in range(20):
+            g.replay()
+            npast.fill_(n0)
+        stream.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(K):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+            torch.cuda.synchronize()
+        barrier(world)
+        dec_ms = e0.elapsed_time(e1)
+        launches = K * (2 * L + 1)
+        assert int(npast.item()) == n0 + K
+        assert kv.error_flags(stream=stream) == 0
+        S_steps = [n0 + i + 1 for i in range(K)]
+        step_bytes = sum(L * (decode_attn_bytes(S) + append_bytes(1)) for S in S_steps) / K
+
+        # ---- the decode-attention kernel alone: 36 launches per replay (roofline)
+        npast.fill_(n0 + K // 2)
+        ga = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ga, stream=stream):
+            for layer in range(L):
+                kv.attn_at(layer, dq[layer], npast, max_keys, SCALE, out=dout[layer], stream=stream)
+        for _ in range(3):
+            ga.replay()
+        stream.synchronize()
+        ra = 20
+        e0.record(stream)
+        for _ in range(ra):
+            ga.replay()
+        e1.record(stream)
+        e1.synchronize()
+        attn_launch_ms = e0.elapsed_time(e1) / (ra * L)
+        S_mid = n0 + K // 2 + 1
+        attn_gbs = decode_attn_bytes(S_mid) / (attn_launch_ms * 1e-3) / 1e9
+
+        # ---- end to end: per step H2D of that step's Q/K/V from pinned memory, the graph,
+        #      D2H of the step's attention output, host waits for the result
+        hq = torch.empty((K, L, 1, NH, HD), dtype=torch.float16).pin_memory()
+        hk = torch.empty((K, L, 1, ne0), dtype=torch.float16).pin_memory()
+        hv = torch.empty((K, L, 1, ne0), dtype=torch.float16).pin_memory()
+        hq.copy_(torch.randn(hq.shape, generator=torch.Generator().manual_seed(SEED)).half())
+        hk.copy_(torch.randn(hk.shape, generator=torch.Generator().manual_seed(SEED + 1)).half())
+        hv.copy_(torch.randn(hv.shape, generator=torch.Generator().manual_seed(SEED + 2)).half())
+        hout = torch.empty((L, 1, NH, HD), dtype=torch.float32).pin_memory()
+        npast.fill_(n0)
+        stream.synchronize()
+        barrier(world)
+        e0.record(stream)
+        for i in range(K):
+            dq.copy_(hq[i], non_blocking=True)
+            dk.copy_(hk[i], non_blocking=True)
+            dvv.copy_(hv[i], non_blocking=True)
+            g.replay()
+            hout.copy_(dout, non_blocking=True)
+            stream.synchronize()
+        e1.record(stream)
+        e1.synchronize()
+        barrier(world)
+        e2e_ms = e0.elapsed_time(e1)
+        h2d = (hq[0].numel() + hk[0].numel() + hv[0].numel()) * 2
+        d2h = hout.numel() * 4
+        assert np.isfinite(hout.numpy()).all()
+
+    dec_ms_max = max_over_ranks(dec_ms, world)
+    e2e_ms_max = max_over_ranks(e2e_ms, world)
+    prefill_ms_max = max_over_ranks(prefill_ms, world)
+    clocks = clk.summary()
+    kv.free()
+    if rank != 0:
+        return
+
+    hbm, tflops_peak, peak_kind = measured_peaks()
+    value = world * K / (dec_ms_max * 1e-3)
+    traffic = profile_traffic("decode_attn_cfg2")
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": dec_ms_max / K,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": {
+            "workload": "BASELINE config 2: 36 layers, 32q/8kv, HD 128, f16 KV cap 8192; turn 2 splices a 384-token "
+                        "tail onto 4096 cached rows, then decode steps at S = 4481..",
+            "sessions_per_gpu": 1,
+            "step": "one decode token through 36 layers (K/V append + causal GQA attention per layer), one CUDA graph",
+            "l2": "inputs larger than L2 (each step reads ~670 MB of K/V)",
+            "parallelism": f"sessions sharded, {world} GPU(s), no data-path collective",
+        },
+        "kv_gbs": world * step_bytes / (dec_ms_max / K * 1e-3) / 1e9,
+        "prefill": {
+            "tflops": world * prefill_flop / (prefill_ms_max * 1e-3) / 1e12,
+            "ms_per_turn": prefill_ms_max,
+            "work": "384-token tail vs 4096 cached rows, 36 layers, 4*NH*HD*sum(visible) = %.3f TFLOP" % (prefill_flop / 1e12),
+            "frac_of_bf16_peak": prefill_tflops / tflops_peak,
+        },
+        "roofline": {
+            "kernel": "fa_decode_kernel<128, f16> (sv_attn_at)",
+            "bound": "hbm",
+            "achieved": attn_gbs,
+            "peak": hbm,
+            "unit": "GB/s",
+            "frac": attn_gbs / hbm,
+            "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+            "bytes_per_launch": decode_attn_bytes(S_mid),
+            "launch_us": attn_launch_ms * 1e3,
+            "traffic": traffic,
+        },
+        "e2e": {"value": world * K / (e2e_ms_max * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "how": "per step: pinned H2D of 36 layers' Q/K/V, graph replay, D2H of the attention output, host sync"},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        n_layers, n_tok = 8, 12
+        per_tl, cores = cpu_decode_sample(n_layers, n_tok)
+        line["cpu_baseline"] = {
+            "value": 1.0 / (per_tl * L), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n_tok} decode tokens through {n_layers} of 36 layers (S~4481), per-token time x{L / n_layers:g}",
+        }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = (1, 0, 0)
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        run_svkv(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

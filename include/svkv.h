@@ -118,6 +118,19 @@ int sv_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t d
 int sv_kv_append(sv_kv* kv, int layer, const void* k, const void* v, int src_type, int n_rows,
                  const int32_t* rows, int base, void* stream);
 
+/* sv_kv_append with the first row read on the device from *base_dev when the
+ * kernel runs (rows *base_dev .. *base_dev + n_rows - 1; a row past n_ctx is
+ * skipped and raises SV_DEVERR_ROW_RANGE).  With sv_attn_at and
+ * sv_counter_add this makes a whole decode step capturable in one CUDA graph
+ * that is replayed unchanged every token -- the purpose of the reference's
+ * static decode graph (src/core/engine/decode_graph.hpp:66-102), without its
+ * 512/1024-row bucket of masked keys. */
+int sv_kv_append_at(sv_kv* kv, int layer, const void* k, const void* v, int src_type, int n_rows,
+                    const int32_t* base_dev, void* stream);
+
+/* *counter_dev += delta on the stream (advances the device-side n_past). */
+int sv_counter_add(int32_t* counter_dev, int delta, void* stream);
+
 /* ================================================================ attention
  * ggml_flash_attn_ext(q, k, v, mask, scale, max_bias = 0, softcap = 0)
  * (llm_block.hpp:268-277) with the reference's views spelled out as ggml
@@ -155,6 +168,13 @@ int sv_flash_attn_ext(const sv_fa_params* p, void* workspace, size_t ws_bytes, v
  * chunked-prefill kernel. */
 int sv_attn(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, int n_past,
             float scale, float* out, void* stream);
+
+/* sv_attn with n_past read on the device from *n_past_dev when the kernel runs
+ * (graph-stable form; see sv_kv_append_at).  max_keys >= n_past + T bounds the
+ * keys any replay may attend and sizes the grid; CTAs past the live length
+ * exit at once, so no masked key is read. */
+int sv_attn_at(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, const int32_t* n_past_dev,
+               int max_keys, float scale, float* out, void* stream);
 
 /* Multi-session attention over one shared cache (vc3_batch.inc:145-172 with
  * set_window_mask, attention.hpp:71-83): query i attends rows [lo[i], hi[i])

@@ -94,6 +94,9 @@ def lib() -> ctypes.CDLL:
         "sv_kv_error": (I, [P, ctypes.POINTER(I), P]),
         "sv_set_rows": (I, [P, I, I64, I64, SZ, P, I, SZ, I64, P, I64, P, P]),
         "sv_kv_append": (I, [P, I, P, P, I, I, P, I, P]),
+        "sv_kv_append_at": (I, [P, I, P, P, I, I, P, P]),
+        "sv_counter_add": (I, [P, I, P]),
+        "sv_attn_at": (I, [P, I, P, I, I, I, P, I, F, P, P]),
         "sv_flash_attn_ext_workspace": (SZ, [ctypes.POINTER(_FaParams)]),
         "sv_flash_attn_ext": (I, [ctypes.POINTER(_FaParams), P, SZ, P]),
         "sv_attn": (I, [P, I, P, I, I, I, I, F, P, P]),
@@ -208,6 +211,24 @@ class KvCache:
         _check("sv_kv_append", lib().sv_kv_append(self.h, layer, _ptr(k), _ptr(v), st, k.shape[0], _ptr(rows), base,
                                                   _stream(stream)))
 
+    def append_at(self, layer: int, k, v, base_dev, stream=None) -> None:
+        """append with the first row read on the device from base_dev (int32 tensor [1])."""
+        import torch
+        st = TYPE_F32 if k.dtype == torch.float32 else TYPE_F16
+        _check("sv_kv_append_at", lib().sv_kv_append_at(self.h, layer, _ptr(k), _ptr(v), st, k.shape[0],
+                                                        _ptr(base_dev), _stream(stream)))
+
+    def attn_at(self, layer: int, q, n_past_dev, max_keys: int, scale: float, out=None, stream=None):
+        """attn with n_past read on the device (graph-capturable)."""
+        import torch
+        T, NH, HD = q.shape
+        if out is None:
+            out = torch.empty((T, NH, HD), dtype=torch.float32, device=q.device)
+        qt = TYPE_F32 if q.dtype == torch.float32 else TYPE_F16
+        _check("sv_attn_at", lib().sv_attn_at(self.h, layer, _ptr(q), qt, T, NH, _ptr(n_past_dev), max_keys, scale,
+                                              _ptr(out), _stream(stream)))
+        return out
+
     def attn(self, layer: int, q, n_past: int, scale: float, out=None, stream=None):
         """Causal attention of q [T, n_head, head_dim] over cache rows [0, n_past + t]."""
         import torch
@@ -241,6 +262,11 @@ class KvCache:
         f = ctypes.c_int()
         _check("sv_kv_error", lib().sv_kv_error(self.h, ctypes.byref(f), _stream(stream)))
         return f.value
+
+
+def counter_add(counter, delta: int, stream=None) -> None:
+    """counter (int32 device tensor [1]) += delta, on the stream."""
+    _check("sv_counter_add", lib().sv_counter_add(_ptr(counter), delta, _stream(stream)))
 
 
 # =================================================================== ggml-op forms

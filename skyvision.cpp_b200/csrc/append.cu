@@ -52,11 +52,11 @@ __global__ void __launch_bounds__(kAppendThreads)
 set_rows_kernel(uint8_t* __restrict__ dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
                 const uint8_t* __restrict__ src, int src_type, size_t src_nb1,
                 const int32_t* __restrict__ rows, int64_t base, int* err,
-                size_t dst_tensor_stride, size_t src_tensor_stride) {
+                size_t dst_tensor_stride, size_t src_tensor_stride, const int32_t* __restrict__ base_dev) {
     extern __shared__ __align__(16) uint8_t qrow[];   // q8_0 row staging
     const int64_t i = blockIdx.x;
     const int z = blockIdx.y;
-    const int64_t r = rows ? (int64_t)rows[i] : base + i;
+    const int64_t r = rows ? (int64_t)rows[i] : (base_dev ? (int64_t)__ldg(base_dev) : base) + i;
     if (r < 0 || r >= dst_rows) {
         if (threadIdx.x == 0 && err) atomicOr(err, ERRBIT_ROW_RANGE);
         return;
@@ -157,12 +157,20 @@ set_rows_kernel(uint8_t* __restrict__ dst, int dst_type, int64_t ne0, int64_t ds
     }
 }
 
+__global__ void counter_add_kernel(int32_t* c, int delta) { *c += delta; }
+
 }  // namespace
+
+cudaError_t launch_counter_add(int32_t* counter, int delta, cudaStream_t st) {
+    counter_add_kernel<<<1, 1, 0, st>>>(counter, delta);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
                             const void* src, int src_type, size_t src_nb1, int64_t n_rows,
                             const int32_t* rows, int64_t base, int* err, int n_tensors,
-                            size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st) {
+                            size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st,
+                            const int32_t* base_dev) {
     if (n_rows <= 0) return cudaSuccess;
     const size_t smem = dst_type == SV_TYPE_Q8_0 ? row_bytes_of(SV_TYPE_Q8_0, ne0) : 0;
     if (smem > 48 * 1024) {
@@ -173,7 +181,7 @@ cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_ro
     dim3 grid((unsigned)n_rows, (unsigned)n_tensors);
     set_rows_kernel<<<grid, kAppendThreads, smem, st>>>(
         static_cast<uint8_t*>(dst), dst_type, ne0, dst_rows, dst_nb1, static_cast<const uint8_t*>(src),
-        src_type, src_nb1, rows, base, err, dst_tensor_stride, src_tensor_stride);
+        src_type, src_nb1, rows, base, err, dst_tensor_stride, src_tensor_stride, base_dev);
     return cudaGetLastError();
 }
 

@@ -98,8 +98,9 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     // ---- key range of this tile and split
     int klo = 0, khi = a.S;
     int wlo = 0, whi = 0, wown = -1;
+    const int cbase = a.causal_base_dev ? __ldg(a.causal_base_dev) : a.causal_base;
     if (a.mask_mode == SV_MASK_CAUSAL) {
-        khi = min(a.S, a.causal_base + t0 + nq);
+        khi = min(a.S, cbase + t0 + nq);
     } else if (a.mask_mode == SV_MASK_WINDOW) {
         wlo = a.lo[t0];
         whi = a.hi[t0];
@@ -180,7 +181,7 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         rvalid[i] = r < R;
         const int qi = r / a.G, g = r % a.G;
         const int t = t0 + qi;
-        rlim[i] = a.causal_base + t;
+        rlim[i] = cbase + t;
         rmask[i] = (a.mask_mode == SV_MASK_EXPLICIT && rvalid[i]) ? a.mask + (size_t)t * a.mask_nb_t : nullptr;
         qrow[i] = rvalid[i] ? a.q + (size_t)t * a.q_nb_t + (size_t)(kvh * a.G + g) * a.q_nb_h : nullptr;
     }

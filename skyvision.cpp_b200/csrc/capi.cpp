@@ -290,6 +290,34 @@ int sv_kv_append(sv_kv* kv, int layer, const void* k, const void* v, int src_typ
     return cuda_status(e);
 }
 
+int sv_kv_append_at(sv_kv* kv, int layer, const void* k, const void* v, int src_type, int n_rows,
+                    const int32_t* base_dev, void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !k || !v || n_rows < 0 || !base_dev) return SV_ERR_INVALID;
+    if (src_type != SV_TYPE_F16 && src_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (n_rows == 0) return SV_OK;
+    DeviceGuard g(kv->device);
+    const int64_t ne0 = (int64_t)kv->n_kv_head * kv->head_dim;
+    const size_t src_nb1 = row_bytes_of(src_type, ne0);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const uint8_t* kb = static_cast<const uint8_t*>(k);
+    const uint8_t* vb = static_cast<const uint8_t*>(v);
+    if (vb > kb)
+        return cuda_status(launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
+                                           src_nb1, n_rows, nullptr, 0, kv->err, 2, kv->tensor_bytes,
+                                           (size_t)(vb - kb), st, base_dev));
+    cudaError_t e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
+                                    src_nb1, n_rows, nullptr, 0, kv->err, 1, 0, 0, st, base_dev);
+    if (e == cudaSuccess)
+        e = launch_set_rows(kv->tensor(layer, 1), kv->type, ne0, kv->n_ctx, kv->row_bytes, v, src_type, src_nb1,
+                            n_rows, nullptr, 0, kv->err, 1, 0, 0, st, base_dev);
+    return cuda_status(e);
+}
+
+int sv_counter_add(int32_t* counter_dev, int delta, void* stream) {
+    if (!counter_dev) return SV_ERR_INVALID;
+    return cuda_status(launch_counter_add(counter_dev, delta, static_cast<cudaStream_t>(stream)));
+}
+
 // ------------------------------------------------------------------ attention
 static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* tv, const CUtensorMap* tkp,
                          const CUtensorMap* tvp, int head_dim, int kv_type, AttnArgs& a, int span, bool window,
@@ -348,6 +376,41 @@ int sv_attn(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, 
     const CUtensorMap* tvp = kv->tm_pre.empty() ? nullptr : &kv->tm_pre[2 * layer + 1];
     return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], tkp, tvp, HD, kv->type, a,
                          n_past + T, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
+                         static_cast<cudaStream_t>(stream));
+}
+
+int sv_attn_at(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, const int32_t* n_past_dev,
+               int max_keys, float scale, float* out, void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !q || !out || T <= 0 || n_head <= 0 || !n_past_dev ||
+        max_keys < T)
+        return SV_ERR_INVALID;
+    if (q_type != SV_TYPE_F16 && q_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (n_head % kv->n_kv_head != 0 || n_head / kv->n_kv_head > 16) return SV_ERR_UNSUPPORTED;
+    if (max_keys > kv->n_ctx) return SV_ERR_OVERFLOW;
+    if (kv->tm_dec.empty()) return SV_ERR_UNSUPPORTED;
+    DeviceGuard g(kv->device);
+    const int HD = kv->head_dim;
+    const int es = q_type == SV_TYPE_F32 ? 4 : 2;
+    AttnArgs a{};
+    a.q = static_cast<const uint8_t*>(q);
+    a.q_type = q_type;
+    a.q_nb_h = (int64_t)HD * es;
+    a.q_nb_t = (int64_t)n_head * HD * es;
+    a.T = T;
+    a.NH = n_head;
+    a.NKV = kv->n_kv_head;
+    a.G = n_head / kv->n_kv_head;
+    a.S = max_keys;
+    a.mask_mode = SV_MASK_CAUSAL;
+    a.causal_base_dev = n_past_dev;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.out = out;
+    a.out_nb_h = HD;
+    a.out_nb_t = (int64_t)n_head * HD;
+    a.err = kv->err;
+    // the device-side base keeps the grid fixed: always the split-K decode kernel
+    return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], nullptr, nullptr, HD, kv->type, a,
+                         max_keys, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
                          static_cast<cudaStream_t>(stream));
 }
 

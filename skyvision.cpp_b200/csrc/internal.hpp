@@ -39,6 +39,7 @@ struct AttnArgs {
     int row_base;           // tensor row of view key 0 (TMA y coordinate offset)
     int mask_mode;
     int causal_base;
+    const int32_t* causal_base_dev;   // when set, the causal base is read on the device (graph-stable)
     const int32_t* lo;      // window mode, device [T]
     const int32_t* hi;
     const int32_t* own;
@@ -105,7 +106,10 @@ cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* t
 cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
                             const void* src, int src_type, size_t src_nb1, int64_t n_rows,
                             const int32_t* rows, int64_t base, int* err, int n_tensors,
-                            size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st);
+                            size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st,
+                            const int32_t* base_dev = nullptr);
+
+cudaError_t launch_counter_add(int32_t* counter, int delta, cudaStream_t st);
 
 cudaError_t launch_compact(KvHandle* kv, const int32_t* seg_dev_unused, const sv_segment* segs, int n_segs,
                            int dst_base, cudaStream_t st);

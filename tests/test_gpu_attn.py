@@ -230,3 +230,53 @@ def test_soft_max_ext(orc, ne0, rows):
     for r in range(rows):
         ref = orc.soft_max_row(x[r], mask[r % 2].view(np.uint16), scale=0.3)
         np.testing.assert_allclose(got[r], ref, rtol=1e-5, atol=1e-7)
+
+
+# ------------------------------------------------------------------ graph-capturable decode step
+def test_device_npast_graph_replay(orc):
+    """sv_kv_append_at + sv_attn_at + sv_counter_add captured once, replayed per token,
+    must equal the eager host-n_past path and the oracle."""
+    NKV, HD, NH, n0, steps = 8, 128, 32, 1000, 5
+    kv = sv.KvCache()
+    assert kv.alloc(0, 2, NKV, HD, 2048)
+    for layer in range(2):
+        fill_cache(orc, kv, layer, n0, seed=8 + layer)
+    ne0 = NKV * HD
+    q = [orc.normal_f16(8, 400 + i, 2 * NH * HD).reshape(2, 1, NH, HD) for i in range(steps)]
+    k = [orc.normal_f16(8, 500 + i, 2 * ne0).reshape(2, 1, ne0) for i in range(steps)]
+    v = [orc.normal_f16(8, 600 + i, 2 * ne0).reshape(2, 1, ne0) for i in range(steps)]
+    td = lambda a: torch.from_numpy(a.view(np.float16)).to(DEV)
+    dq, dk, dv = td(q[0]).clone(), td(k[0]).clone(), td(v[0]).clone()
+    dout = torch.zeros(2, 1, NH, HD, dtype=torch.float32, device=DEV)
+    npast = torch.full((1,), n0, dtype=torch.int32, device=DEV)
+    st = torch.cuda.Stream()
+    max_keys = n0 + steps + 3
+
+    def step():
+        for layer in range(2):
+            kv.append_at(layer, dk[layer], dv[layer], npast, stream=st)
+            kv.attn_at(layer, dq[layer], npast, max_keys, 1 / np.sqrt(HD), out=dout[layer], stream=st)
+        sv.counter_add(npast, 1, stream=st)
+
+    with torch.cuda.stream(st):
+        step()                              # eager warm-up writes row n0; rewind
+        st.synchronize()
+        npast.fill_(n0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            step()
+        st.synchronize()
+        for i in range(steps):
+            dq.copy_(td(q[i]))
+            dk.copy_(td(k[i]))
+            dv.copy_(td(v[i]))
+            g.replay()
+            st.synchronize()
+            got = dout.cpu().numpy()
+            for layer in range(2):
+                kc = kv.tensor(layer, 0).cpu().numpy()
+                assert np.array_equal(kc[n0 + i].view(np.uint16), k[i][layer, 0])
+                ref = ref_attn(orc, kv, layer, q[i][layer], n0 + i, 1 / np.sqrt(HD))
+                close(got[layer], ref)
+    assert int(npast.item()) == n0 + steps
+    assert kv.error_flags() == 0
