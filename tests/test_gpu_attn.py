@@ -125,6 +125,24 @@ def test_short_chunks(orc, T, n_past):
     close(out.cpu().numpy(), ref_attn(orc, kv, 1, q, n_past, 1 / np.sqrt(128)))
 
 
+@pytest.mark.parametrize("hd,nkv,nh,T,n_past", [
+    (128, 8, 32, 384, 4096),     # BASELINE config 2 splice tail: 384 new rows over 4096 cached
+    (128, 8, 32, 128, 0),        # first chunk of a prompt
+    (256, 4, 16, 512, 1024),     # config 4 geometry (f16 cache), a 512-token chunk
+    (128, 2, 2, 200, 37),        # GQA 1:1 -> 128 queries per tile, ragged last tile
+    (128, 8, 64, 70, 500),       # GQA 8:1 -> 16 queries per tile
+])
+def test_prefill_chunks(orc, hd, nkv, nh, T, n_past):
+    """Chunked prefill (query rows > 16 per kv head) on the tcgen05 kernel."""
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, nkv, hd, n_past + T + 64)
+    fill_cache(orc, kv, 0, n_past + T, seed=11)
+    q = orc.normal_f16(11, 1000 + T, T * nh * hd).reshape(T, nh, hd)
+    out = kv.attn(0, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / np.sqrt(hd))
+    close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n_past, 1 / np.sqrt(hd)))
+    assert kv.error_flags() == 0
+
+
 @pytest.mark.parametrize("hd,nkv,nh", [(64, 4, 16), (256, 4, 16), (128, 8, 8), (128, 2, 32), (32, 8, 8), (16, 2, 8)])
 def test_decode_head_geometries(orc, hd, nkv, nh):
     kv = sv.KvCache()
