@@ -159,6 +159,19 @@ typedef struct sv_fa_params {
 size_t sv_flash_attn_ext_workspace(const sv_fa_params* p);
 int sv_flash_attn_ext(const sv_fa_params* p, void* workspace, size_t ws_bytes, void* stream);
 
+/* sv_flash_attn_ext without a workspace argument: the split-K scratch is a
+ * 4 MiB static device array inside this library (held by every GPU that loads
+ * it until the process exits), for callers that cannot allocate device memory
+ * where attention runs -- e.g. an operator inside a ggml backend graph, which
+ * receives only its tensors, or code running during CUDA stream capture.
+ * No counterpart in the reference.  The first call on a device resolves the
+ * array's address (cudaGetSymbolAddress) with that device current: make it
+ * before any stream capture.  Shapes that need more than 4 MiB of scratch
+ * return SV_ERR_WORKSPACE.  The array is shared by all calls and keeps the last
+ * call's contents (the merge tickets are cleared on each call); calls that
+ * overlap on the GPU race. */
+int sv_flash_attn_ext_static(const sv_fa_params* p, void* stream);
+
 /* Cache-level attention for one decoder layer (the FA node of
  * qwen3vl_model.cpp:657-663 with the causal mask of set_causal_mask(mask,
  * n_past, T) computed in-kernel): query t (0 <= t < T) attends cache rows
