@@ -317,9 +317,10 @@ def run_svkv(args, world, rank, local):
         dout = torch.empty(L, 1, NH, HD, dtype=torch.float32, device=dev)
 
         def step():
+            # per layer: the fused append + attention kernel (one launch), then the n_past advance
             for layer in range(L):
-                kv.append_at(layer, dk[layer], dvv[layer], npast, stream=stream)
-                kv.attn_at(layer, dq[layer], npast, max_keys, SCALE, out=dout[layer], stream=stream)
+                kv.attn_append_at(layer, dq[layer], dk[layer], dvv[layer], npast, max_keys, SCALE, out=dout[layer],
+                                  stream=stream)
             sv.counter_add(npast, 1, stream=stream)
 
         step()                                     # eager run before capture (sets kernel attributes)
@@ -349,7 +350,7 @@ def run_svkv(args, world, rank, local):
             torch.cuda.synchronize()
         barrier(world)
         dec_ms = e0.elapsed_time(e1)
-        launches = K * (2 * L + 1)
+        launches = K * (L + 1)
         assert int(npast.item()) == n0 + K
         assert kv.error_flags(stream=stream) == 0
         S_steps = [n0 + i + 1 for i in range(K)]
@@ -360,7 +361,8 @@ def run_svkv(args, world, rank, local):
         ga = torch.cuda.CUDAGraph()
         with torch.cuda.graph(ga, stream=stream):
             for layer in range(L):
-                kv.attn_at(layer, dq[layer], npast, max_keys, SCALE, out=dout[layer], stream=stream)
+                kv.attn_append_at(layer, dq[layer], dk[layer], dvv[layer], npast, max_keys, SCALE, out=dout[layer],
+                                  stream=stream)
         for _ in range(3):
             ga.replay()
         stream.synchronize()
@@ -372,7 +374,8 @@ def run_svkv(args, world, rank, local):
         e1.synchronize()
         attn_launch_ms = e0.elapsed_time(e1) / (ra * L)
         S_mid = n0 + K // 2 + 1
-        attn_gbs = decode_attn_bytes(S_mid) / (attn_launch_ms * 1e-3) / 1e9
+        attn_launch_bytes = decode_attn_bytes(S_mid) + append_bytes(1)
+        attn_gbs = attn_launch_bytes / (attn_launch_ms * 1e-3) / 1e9
 
         # ---- end to end: per step H2D of that step's Q/K/V from pinned memory, the graph,
         #      D2H of the step's attention output, host waits for the result
@@ -430,7 +433,7 @@ def run_svkv(args, world, rank, local):
             "workload": "BASELINE config 2: 36 layers, 32q/8kv, HD 128, f16 KV cap 8192; turn 2 splices a 384-token "
                         "tail onto 4096 cached rows, then decode steps at S = 4481..",
             "sessions_per_gpu": 1,
-            "step": "one decode token through 36 layers (K/V append + causal GQA attention per layer), one CUDA graph",
+            "step": "one decode token through 36 layers (fused K/V append + causal GQA attention, one kernel per layer), one CUDA graph",
             "l2": "inputs larger than L2 (each step reads ~670 MB of K/V)",
             "parallelism": f"sessions sharded, {world} GPU(s), no data-path collective",
         },
@@ -442,14 +445,14 @@ def run_svkv(args, world, rank, local):
             "frac_of_bf16_peak": prefill_tflops / tflops_peak,
         },
         "roofline": {
-            "kernel": "fa_decode_kernel<128, f16> (sv_attn_at)",
+            "kernel": "fa_decode_kernel<128, f16> fused append + attention (sv_attn_append_at)",
             "bound": "hbm",
             "achieved": attn_gbs,
             "peak": hbm,
             "unit": "GB/s",
             "frac": attn_gbs / hbm,
             "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-            "bytes_per_launch": decode_attn_bytes(S_mid),
+            "bytes_per_launch": attn_launch_bytes,
             "launch_us": attn_launch_ms * 1e3,
             "traffic": traffic,
         },

@@ -189,6 +189,17 @@ int sv_attn(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, 
 int sv_attn_at(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, const int32_t* n_past_dev,
                int max_keys, float scale, float* out, void* stream);
 
+/* The two ops a decoder layer emits per token fused into one kernel: the K/V
+ * append (ggml_set_rows of k_new/v_new at rows *n_past_dev + t,
+ * qwen3vl_model.cpp:654-655) and the causal attention over the cache including
+ * those rows (qwen3vl_model.cpp:657-663).  k_new/v_new: device f16
+ * [T][n_kv_head*head_dim].  f16 caches with T*(n_head/n_kv_head) <= 16 run as
+ * one kernel (the CTA that covers a new row writes it to the cache and uses it
+ * from shared memory); other cases run sv_kv_append_at then sv_attn_at.
+ * Graph-stable like sv_attn_at. */
+int sv_attn_append_at(sv_kv* kv, int layer, const void* q, int q_type, const void* k_new, const void* v_new, int T,
+                      int n_head, const int32_t* n_past_dev, int max_keys, float scale, float* out, void* stream);
+
 /* Multi-session attention over one shared cache (vc3_batch.inc:145-172 with
  * set_window_mask, attention.hpp:71-83): query i attends rows [lo[i], hi[i])
  * plus row own[i].  lo/hi/own: device int32 [n_q]; max_span: an upper bound

@@ -97,6 +97,7 @@ def lib() -> ctypes.CDLL:
         "sv_kv_append_at": (I, [P, I, P, P, I, I, P, P]),
         "sv_counter_add": (I, [P, I, P]),
         "sv_attn_at": (I, [P, I, P, I, I, I, P, I, F, P, P]),
+        "sv_attn_append_at": (I, [P, I, P, I, P, P, I, I, P, I, F, P, P]),
         "sv_flash_attn_ext_workspace": (SZ, [ctypes.POINTER(_FaParams)]),
         "sv_flash_attn_ext": (I, [ctypes.POINTER(_FaParams), P, SZ, P]),
         "sv_attn": (I, [P, I, P, I, I, I, I, F, P, P]),
@@ -227,6 +228,19 @@ class KvCache:
         qt = TYPE_F32 if q.dtype == torch.float32 else TYPE_F16
         _check("sv_attn_at", lib().sv_attn_at(self.h, layer, _ptr(q), qt, T, NH, _ptr(n_past_dev), max_keys, scale,
                                               _ptr(out), _stream(stream)))
+        return out
+
+    def attn_append_at(self, layer: int, q, k_new, v_new, n_past_dev, max_keys: int, scale: float, out=None,
+                       stream=None):
+        """Fused decode step of one layer: append k_new/v_new at *n_past_dev and attend (graph-capturable)."""
+        import torch
+        T, NH, HD = q.shape
+        if out is None:
+            out = torch.empty((T, NH, HD), dtype=torch.float32, device=q.device)
+        qt = TYPE_F32 if q.dtype == torch.float32 else TYPE_F16
+        _check("sv_attn_append_at", lib().sv_attn_append_at(self.h, layer, _ptr(q), qt, _ptr(k_new), _ptr(v_new), T,
+                                                            NH, _ptr(n_past_dev), max_keys, scale, _ptr(out),
+                                                            _stream(stream)))
         return out
 
     def attn(self, layer: int, q, n_past: int, scale: float, out=None, stream=None):

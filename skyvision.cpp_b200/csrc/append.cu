@@ -54,6 +54,8 @@ set_rows_kernel(uint8_t* __restrict__ dst, int dst_type, int64_t ne0, int64_t ds
                 const int32_t* __restrict__ rows, int64_t base, int* err,
                 size_t dst_tensor_stride, size_t src_tensor_stride, const int32_t* __restrict__ base_dev) {
     extern __shared__ __align__(16) uint8_t qrow[];   // q8_0 row staging
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
     const int64_t i = blockIdx.x;
     const int z = blockIdx.y;
     const int64_t r = rows ? (int64_t)rows[i] : (base_dev ? (int64_t)__ldg(base_dev) : base) + i;
@@ -157,13 +159,16 @@ set_rows_kernel(uint8_t* __restrict__ dst, int dst_type, int64_t ne0, int64_t ds
     }
 }
 
-__global__ void counter_add_kernel(int32_t* c, int delta) { *c += delta; }
+__global__ void counter_add_kernel(int32_t* c, int delta) {
+    pdl_wait();
+    *c += delta;
+    pdl_trigger();
+}
 
 }  // namespace
 
 cudaError_t launch_counter_add(int32_t* counter, int delta, cudaStream_t st) {
-    counter_add_kernel<<<1, 1, 0, st>>>(counter, delta);
-    return cudaGetLastError();
+    return launch_pdl(counter_add_kernel, dim3(1), dim3(1), 0, st, counter, delta);
 }
 
 cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
@@ -179,10 +184,9 @@ cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_ro
         if (e != cudaSuccess) return e;
     }
     dim3 grid((unsigned)n_rows, (unsigned)n_tensors);
-    set_rows_kernel<<<grid, kAppendThreads, smem, st>>>(
-        static_cast<uint8_t*>(dst), dst_type, ne0, dst_rows, dst_nb1, static_cast<const uint8_t*>(src),
-        src_type, src_nb1, rows, base, err, dst_tensor_stride, src_tensor_stride, base_dev);
-    return cudaGetLastError();
+    return launch_pdl(set_rows_kernel, grid, dim3(kAppendThreads), smem, st, static_cast<uint8_t*>(dst), dst_type, ne0,
+                      dst_rows, dst_nb1, static_cast<const uint8_t*>(src), src_type, src_nb1, rows, base, err,
+                      dst_tensor_stride, src_tensor_stride, base_dev);
 }
 
 }  // namespace svkv

@@ -52,14 +52,18 @@ struct DecCfg {
     static constexpr int BOXB = kBK * PITCH;
     static constexpr int HEADB = Q8 ? HD / kQK8_0 * kQ8_0Bytes : HD * 2;
     static constexpr int TILE_B = Q8 ? kBK * HEADB : NB * BOXB;   // K (or V) bytes per stage
-    static constexpr int STAGES = (HD >= 256) ? 3 : 4;
+    static constexpr int STAGES = 3;                              // HD <= 128: two CTAs fit per SM
+    static constexpr int MIN_BLOCKS = HD >= 256 ? 1 : 2;
     static constexpr int STAGE_B = align_up(2 * TILE_B, 1024);
     static constexpr int WBOXB = 16 * PITCH;                      // q8 staging box (16 keys)
     static constexpr int WSTAGE_B = Q8 ? 2 * NB * WBOXB : 0;      // per warp: K and V f16 tiles
     static constexpr int NBLK = HD / kQK8_0;
     static constexpr int WD_B = Q8 ? 2 * 16 * NBLK * 4 : 0;       // per warp: dK, dV tables
     static constexpr int RING_B = STAGES * STAGE_B;
-    static constexpr int COMB_B = kConsumerWarps * 16 * HD * 4 + kConsumerWarps * 16 * 2 * 4;
+    static constexpr int COMB_B = kConsumerWarps * 16 * HD * 4 + (kConsumerWarps * 16 * 2 + 16 * kConsumerWarps + 32) * 4;
+    static constexpr int PO_OFF = align_up(COMB_B, 16);             // cluster merge: this CTA's partial O
+    static constexpr int PM_OFF = PO_OFF + 16 * HD * 4;              //                and its (m, l) per row
+    static_assert(PM_OFF + 16 * 2 * 4 <= RING_B, "cluster-merge partials must fit in the stage ring");
     static constexpr int BAR_OFF = RING_B + kConsumerWarps * (WSTAGE_B + WD_B);
     static constexpr int SMEM = BAR_OFF + 2 * STAGES * 8 + 16;
     static_assert(COMB_B <= RING_B, "combine scratch must fit in the stage ring");
@@ -79,7 +83,7 @@ __device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w) {
 }
 
 template <int HD, int KVT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, DecCfg<HD, KVT>::MIN_BLOCKS)
 fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                  const __grid_constant__ AttnArgs a) {
     using C = DecCfg<HD, KVT>;
@@ -94,6 +98,54 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     const int t0 = qt * a.qpt;
     const int nq = min(a.qpt, a.T - t0);
     const int R = nq * a.G;
+
+    // prologue that touches no global memory overlaps the previous kernel (PDL)
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        flag[0] = 0;
+        flag[1] = 0;
+        fence_barrier_init();
+    }
+    if (threadIdx.x == kConsumerWarps * 32) {
+        tma_prefetch_desc(&tmk);
+        tma_prefetch_desc(&tmv);
+    }
+    __syncthreads();
+
+    // one stage of K and V tiles for keys [y, y + kBK) of this kv head
+    auto issue = [&](int j, int y) {
+        const int s = j % C::STAGES;
+        uint8_t* kst = smem + s * C::STAGE_B;
+        uint8_t* vst = kst + C::TILE_B;
+        mbar_arrive_expect_tx(&full[s], 2 * C::TILE_B);
+        if constexpr (C::Q8) {
+            tma_load_2d(kst, &tmk, kvh * (C::HEADB / 2), y, &full[s]);
+            tma_load_2d(vst, &tmv, kvh * (C::HEADB / 2), y, &full[s]);
+        } else {
+#pragma unroll
+            for (int b = 0; b < C::NB; b++) {
+                tma_load_2d(kst + b * C::BOXB, &tmk, kvh * HD + b * C::COLS, y, &full[s]);
+                tma_load_2d(vst + b * C::BOXB, &tmv, kvh * HD + b * C::COLS, y, &full[s]);
+            }
+        }
+    };
+    // A kernel that appends its own new rows (fused decode step) starts streaming its split's
+    // first tiles before waiting for the previous kernel: the rows it reads were completed by
+    // earlier steps, and the rows it appends are patched in from their source below.  The
+    // split's start does not depend on n_past in causal mode, only its end does.
+    int prefetched = 0;
+    if (a.n_new > 0 && a.mask_mode == SV_MASK_CAUSAL && threadIdx.x == kConsumerWarps * 32) {
+        const int ks0 = split * a.chunk;
+        const int kmax = min(a.S, ks0 + a.chunk);
+        const int nt_max = kmax > ks0 ? (kmax - ks0 + kBK - 1) / kBK : 0;
+        prefetched = min(nt_max, C::STAGES);
+        for (int j = 0; j < prefetched; j++) issue(j, a.row_base + ks0 + j * kBK);
+    }
+    pdl_wait();
+    if (threadIdx.x == 0) pdl_trigger();
 
     // ---- key range of this tile and split
     int klo = 0, khi = a.S;
@@ -117,51 +169,33 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     const int ks = klo + split * a.chunk;
     const int ke = min(khi, ks + a.chunk);
     const int n_tiles = ke > ks ? (ke - ks + kBK - 1) / kBK : 0;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < C::STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        flag[0] = 0;
-        flag[1] = 0;
-        fence_barrier_init();
-    }
-    __syncthreads();
+    if (a.n_new > 0 && cbase + a.n_new > a.S && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 &&
+        blockIdx.z == 0 && a.err)
+        atomicOr(a.err, ERRBIT_ROW_RANGE);   // appended rows past the grid's key bound are not written
 
     if (warp == kConsumerWarps) {
         // ============================ TMA producer
-        if (lane == 0 && n_tiles > 0) {
-            tma_prefetch_desc(&tmk);
-            tma_prefetch_desc(&tmv);
-            int issued = 0;
-            for (int j = 0; j < n_tiles; j++) {
+        if (lane == 0 && (n_tiles > 0 || prefetched > 0)) {
+            int issued = prefetched;
+            for (int j = prefetched; j < n_tiles; j++) {
                 const int s = j % C::STAGES;
                 if (j >= C::STAGES && !mbar_wait(&empty[s], ((j / C::STAGES) - 1) & 1, a.err)) {
                     flag[0] = 1;
                     break;
                 }
                 if (flag[0]) break;
-                uint8_t* kst = smem + s * C::STAGE_B;
-                uint8_t* vst = kst + C::TILE_B;
-                mbar_arrive_expect_tx(&full[s], 2 * C::TILE_B);
-                const int y = a.row_base + ks + j * kBK;
-                if constexpr (C::Q8) {
-                    tma_load_2d(kst, &tmk, kvh * (C::HEADB / 2), y, &full[s]);
-                    tma_load_2d(vst, &tmv, kvh * (C::HEADB / 2), y, &full[s]);
-                } else {
-#pragma unroll
-                    for (int b = 0; b < C::NB; b++) {
-                        tma_load_2d(kst + b * C::BOXB, &tmk, kvh * HD + b * C::COLS, y, &full[s]);
-                        tma_load_2d(vst + b * C::BOXB, &tmv, kvh * HD + b * C::COLS, y, &full[s]);
-                    }
-                }
+                issue(j, a.row_base + ks + j * kBK);
                 issued = j + 1;
             }
             // never leave a bulk copy in flight into shared memory: wait (bounded) for the
             // last phase of every stage this thread filled
             for (int j = max(0, issued - C::STAGES); j < issued; j++)
                 mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, a.err);
+        }
+        if (a.cluster_merge) {      // the producer warp takes part in the two cluster barriers of the merge
+            __syncwarp();
+            cluster_sync_all();
+            cluster_sync_all();
         }
         return;
     }
@@ -227,6 +261,31 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         if (kw < ke) {
             const uint8_t* kst = smem + s * C::STAGE_B;
             const uint8_t* vst = kst + C::TILE_B;
+            if constexpr (!C::Q8) {
+                // fused append (f16 cache): a key this launch appends is written to the cache from its
+                // source row and patched into the tile the TMA brought in (which may hold the old row)
+                if (a.n_new > 0 && kw < cbase + a.n_new && kw + 16 > cbase) {
+                    constexpr int LANES = HD * 2 / 16;             // 16-byte pieces of one head's row
+                    const int k_lo = max(kw, cbase), k_hi = min(kw + 16, cbase + a.n_new);
+                    for (int key = k_lo; key < k_hi; key++) {
+                        if (lane < LANES) {
+                            const size_t so = (size_t)(key - cbase) * a.new_nb_t + (size_t)kvh * HD * 2 + lane * 16;
+                            const uint4 kvec = *reinterpret_cast<const uint4*>(a.knew + so);
+                            const uint4 vvec = *reinterpret_cast<const uint4*>(a.vnew + so);
+                            const size_t co = (size_t)key * a.cache_row_bytes + (size_t)kvh * HD * 2 + lane * 16;
+                            *reinterpret_cast<uint4*>(a.kc_w + co) = kvec;
+                            *reinterpret_cast<uint4*>(a.vc_w + co) = vvec;
+                            const int row = key - (ks + j * kBK);
+                            const int e = lane * 8;
+                            const uint32_t off = (e / C::COLS) * C::BOXB + swz_off(row, e % C::COLS, C::PITCH);
+                            *reinterpret_cast<uint4*>(const_cast<uint8_t*>(kst) + off) = kvec;
+                            *reinterpret_cast<uint4*>(const_cast<uint8_t*>(vst) + off) = vvec;
+                        }
+                    }
+                    fence_proxy_async_smem();   // order these writes before the stage's next TMA fill
+                    __syncwarp();
+                }
+            }
             float sacc[2][4];
 #pragma unroll
             for (int nt = 0; nt < 2; nt++) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
@@ -411,14 +470,20 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
     }
     consumer_sync();   // every warp is done with the stage ring: reuse it
-    float* cw = reinterpret_cast<float*>(smem);               // [4][16][HD]
-    float* cm = cw + kConsumerWarps * 16 * HD;                 // [4][16]
-    float* cl = cm + kConsumerWarps * 16;
+    float* cw = reinterpret_cast<float*>(smem);               // [4][16][HD] warp partials
+    float* cm = cw + kConsumerWarps * 16 * HD;                 // [4][16] warp maxima
+    float* cl = cm + kConsumerWarps * 16;                      // [4][16] warp sums
+    float* rs = cl + kConsumerWarps * 16;                      // [16][4] per-row warp weights (unnormalised)
+    float* rm = rs + 16 * kConsumerWarps;                      // [16][2] per-row (M, L)
+    if (rrow[0] < R) {
 #pragma unroll
-    for (int n = 0; n < HD / 8; n++) {
-        const int col = n * 8 + 2 * q4;
-        *reinterpret_cast<float2*>(&cw[(warp * 16 + rrow[0]) * HD + col]) = make_float2(o[n][0], o[n][1]);
-        *reinterpret_cast<float2*>(&cw[(warp * 16 + rrow[1]) * HD + col]) = make_float2(o[n][2], o[n][3]);
+        for (int n = 0; n < HD / 8; n++)
+            *reinterpret_cast<float2*>(&cw[(warp * 16 + rrow[0]) * HD + n * 8 + 2 * q4]) = make_float2(o[n][0], o[n][1]);
+    }
+    if (rrow[1] < R) {
+#pragma unroll
+        for (int n = 0; n < HD / 8; n++)
+            *reinterpret_cast<float2*>(&cw[(warp * 16 + rrow[1]) * HD + n * 8 + 2 * q4]) = make_float2(o[n][2], o[n][3]);
     }
     if (q4 == 0) {
         cm[warp * 16 + rrow[0]] = m[0];
@@ -427,54 +492,110 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
         cl[warp * 16 + rrow[1]] = l[1];
     }
     consumer_sync();
-
-    constexpr int CPT = HD / 8;                   // columns per thread (8 threads per row)
-    const int r = tid >> 3;
-    const int c0 = (tid & 7) * CPT;
-    const int tile = qt * a.NKV + kvh;
-    float M = -INFINITY, L = 0.0f;
-    float acc[CPT];
+    if (tid < R) {
+        float M = -INFINITY, L = 0.0f;
 #pragma unroll
-    for (int c = 0; c < CPT; c++) acc[c] = 0.0f;
-    if (r < R) {
-        float sc[kConsumerWarps];
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; w++) M = fmaxf(M, cm[w * 16 + r]);
+        for (int w = 0; w < kConsumerWarps; w++) M = fmaxf(M, cm[w * 16 + tid]);
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; w++) {
-            const float mw = cm[w * 16 + r];
-            sc[w] = mw == -INFINITY ? 0.0f : fast_exp2(mw - M);
-            L += cl[w * 16 + r] * sc[w];
+            const float mw = cm[w * 16 + tid];
+            const float sc = mw == -INFINITY ? 0.0f : fast_exp2(mw - M);
+            rs[tid * kConsumerWarps + w] = sc;
+            L += cl[w * 16 + tid] * sc;
         }
-#pragma unroll
-        for (int c = 0; c < CPT; c++) {
-            float v = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; w++) v += cw[(w * 16 + r) * HD + c0 + c] * sc[w];
-            acc[c] = v;
-        }
+        rm[tid * 2] = M;
+        rm[tid * 2 + 1] = L;
     }
-    const int qi = r / a.G, g = r % a.G;
-    float* orow = (r < R) ? a.out + (size_t)(t0 + qi) * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h : nullptr;
+    consumer_sync();
 
+    // each thread owns float4 column groups of the R live rows
+    constexpr int G4 = HD / 4;
+    const int tile = qt * a.NKV + kvh;
+    const int n_g = R * G4;
     if (a.n_splits == 1) {
-        if (r < R) {
-            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        for (int gi = tid; gi < n_g; gi += kConsumerWarps * 32) {
+            const int r = gi / G4, c = (gi % G4) * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-            for (int c = 0; c < CPT; c++) orow[c0 + c] = acc[c] * inv;
+            for (int w = 0; w < kConsumerWarps; w++) {
+                const float sc = rs[r * kConsumerWarps + w];
+                const float4 v = *reinterpret_cast<const float4*>(&cw[(w * 16 + r) * HD + c]);
+                acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
+            }
+            const float L = rm[r * 2 + 1];
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            const int qi = r / a.G, g = r % a.G;
+            float* orow = a.out + (size_t)(t0 + qi) * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
+            *reinterpret_cast<float4*>(orow + c) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
         }
         return;
     }
-    // ---- split-K: publish the partial, the last CTA of the tile merges
-    const size_t pidx = ((size_t)tile * a.n_splits + split) * 16 + r;
-    if (r < R) {
+    if (a.cluster_merge) {
+        // ---- split-K inside a thread-block cluster: every split keeps its partial in its own
+        // shared memory; after a cluster barrier each CTA merges a slice of the columns by
+        // reading all splits' partials through distributed shared memory.
+        float* po = reinterpret_cast<float*>(smem + C::PO_OFF);   // [16][HD]
+        float* pm = reinterpret_cast<float*>(smem + C::PM_OFF);   // [16][2]
+        for (int gi = tid; gi < n_g; gi += kConsumerWarps * 32) {
+            const int r = gi / G4, c = (gi % G4) * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < CPT; c++) a.ws_o[pidx * HD + c0 + c] = acc[c];
-        if ((tid & 7) == 0) {
-            a.ws_ml[pidx * 2 + 0] = M;
-            a.ws_ml[pidx * 2 + 1] = L;
+            for (int w = 0; w < kConsumerWarps; w++) {
+                const float sc = rs[r * kConsumerWarps + w];
+                const float4 v = *reinterpret_cast<const float4*>(&cw[(w * 16 + r) * HD + c]);
+                acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
+            }
+            *reinterpret_cast<float4*>(&po[r * HD + c]) = acc;
         }
+        if (tid < R) *reinterpret_cast<float2*>(&pm[tid * 2]) = make_float2(rm[tid * 2], rm[tid * 2 + 1]);
+        cluster_sync_all();
+        const int ns = a.n_splits;                    // == cluster size, rank == split
+        const uint32_t rank = cluster_ctarank();
+        for (int gi = (int)rank + ns * tid; gi < n_g; gi += ns * kConsumerWarps * 32) {
+            const int r = gi / G4, c = (gi % G4) * 4;
+            float2 ml[16];
+            float4 ov[16];
+            float M = -INFINITY;
+#pragma unroll
+            for (int sp = 0; sp < 16; sp++) {
+                if (sp < ns) {
+                    ml[sp] = dsmem_ld_f2(dsmem_map(smem_u32(&pm[r * 2]), sp));
+                    ov[sp] = dsmem_ld_f4(dsmem_map(smem_u32(&po[r * HD + c]), sp));
+                    M = fmaxf(M, ml[sp].x);
+                }
+            }
+            float L = 0.0f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int sp = 0; sp < 16; sp++) {
+                if (sp < ns && ml[sp].x != -INFINITY) {
+                    const float w = fast_exp2(ml[sp].x - M);
+                    L += ml[sp].y * w;
+                    acc.x += ov[sp].x * w; acc.y += ov[sp].y * w; acc.z += ov[sp].z * w; acc.w += ov[sp].w * w;
+                }
+            }
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            const int qi = r / a.G, g = r % a.G;
+            float* orow = a.out + (size_t)(t0 + qi) * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
+            *reinterpret_cast<float4*>(orow + c) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
+        cluster_sync_all();                          // keep every CTA's partial alive until all reads are done
+        return;
     }
+    // ---- split-K: publish the partial, the last CTA of the tile merges
+    const size_t pbase = ((size_t)tile * a.n_splits + split) * 16;
+    for (int gi = tid; gi < n_g; gi += kConsumerWarps * 32) {
+        const int r = gi / G4, c = (gi % G4) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; w++) {
+            const float sc = rs[r * kConsumerWarps + w];
+            const float4 v = *reinterpret_cast<const float4*>(&cw[(w * 16 + r) * HD + c]);
+            acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
+        }
+        *reinterpret_cast<float4*>(&a.ws_o[(pbase + r) * HD + c]) = acc;
+    }
+    if (tid < R) *reinterpret_cast<float2*>(&a.ws_ml[(pbase + tid) * 2]) = make_float2(rm[tid * 2], rm[tid * 2 + 1]);
     __threadfence();
     consumer_sync();
     if (tid == 0) {
@@ -484,45 +605,119 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     consumer_sync();
     if (!flag[1]) return;
     __threadfence();
-    if (r < R) {
-        float MM = -INFINITY;
-        for (int sp = 0; sp < a.n_splits; sp++)
-            MM = fmaxf(MM, __ldcg(&a.ws_ml[(((size_t)tile * a.n_splits + sp) * 16 + r) * 2]));
-        float LL = 0.0f;
+    // per (row, split) weights w = exp2(m_s - M) / L, computed once into shared memory
+    const int ns = a.n_splits;
+    float* wgt = reinterpret_cast<float*>(smem);               // [16][ns] (the stage ring is free)
+    const size_t tbase = (size_t)tile * ns * 16;
+    for (int r = warp; r < R; r += kConsumerWarps) {
+        float M = -INFINITY;
+        for (int sp = lane; sp < ns; sp += 32) M = fmaxf(M, __ldcg(&a.ws_ml[(tbase + (size_t)sp * 16 + r) * 2]));
 #pragma unroll
-        for (int c = 0; c < CPT; c++) acc[c] = 0.0f;
-        for (int sp = 0; sp < a.n_splits; sp++) {
-            const size_t pi = ((size_t)tile * a.n_splits + sp) * 16 + r;
-            const float ms = __ldcg(&a.ws_ml[pi * 2]);
-            if (ms == -INFINITY) continue;
-            const float w = fast_exp2(ms - MM);
-            LL += __ldcg(&a.ws_ml[pi * 2 + 1]) * w;
-#pragma unroll
-            for (int c = 0; c < CPT; c++) acc[c] += __ldcg(&a.ws_o[pi * HD + c0 + c]) * w;
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+        float L = 0.0f;
+        for (int sp = lane; sp < ns; sp += 32) {
+            const float2 ml = __ldcg(reinterpret_cast<const float2*>(&a.ws_ml[(tbase + (size_t)sp * 16 + r) * 2]));
+            const float w = ml.x == -INFINITY ? 0.0f : fast_exp2(ml.x - M);
+            wgt[r * ns + sp] = w;
+            L += ml.y * w;
         }
-        const float inv = LL > 0.0f ? 1.0f / LL : 0.0f;
 #pragma unroll
-        for (int c = 0; c < CPT; c++) orow[c0 + c] = acc[c] * inv;
+        for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        __syncwarp();
+        for (int sp = lane; sp < ns; sp += 32) wgt[r * ns + sp] *= inv;
+    }
+    consumer_sync();
+    for (int gi = tid; gi < n_g; gi += kConsumerWarps * 32) {
+        const int r = gi / G4, c = (gi % G4) * 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        int sp = 0;
+        for (; sp + 4 <= ns; sp += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                v[u] = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[(tbase + (size_t)(sp + u) * 16 + r) * HD + c]));
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float w = wgt[r * ns + sp + u];
+                acc.x += v[u].x * w; acc.y += v[u].y * w; acc.z += v[u].z * w; acc.w += v[u].w * w;
+            }
+        }
+        for (; sp < ns; sp++) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[(tbase + (size_t)sp * 16 + r) * HD + c]));
+            const float w = wgt[r * ns + sp];
+            acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+        }
+        const int qi = r / a.G, g = r % a.G;
+        float* orow = a.out + (size_t)(t0 + qi) * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
+        *reinterpret_cast<float4*>(orow + c) = acc;
     }
     if (tid == 0) a.tickets[tile] = 0;
+}
+
+// one-time kernel attributes: dynamic shared memory and clusters of up to 16 CTAs
+template <int HD, int KVT>
+cudaError_t prepare_t() {
+    static cudaError_t status = [] {
+        using C = DecCfg<HD, KVT>;
+        cudaError_t e = cudaFuncSetAttribute(fa_decode_kernel<HD, KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             C::SMEM + 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fa_decode_kernel<HD, KVT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        return e;
+    }();
+    return status;
 }
 
 template <int HD, int KVT>
 cudaError_t launch_t(const AttnArgs& a, const CUtensorMap* tk, const CUtensorMap* tv, cudaStream_t st) {
     using C = DecCfg<HD, KVT>;
-    static bool attr_set = false;
     const int smem = C::SMEM + 1024;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(fa_decode_kernel<HD, KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    cudaError_t e = prepare_t<HD, KVT>();
+    if (e != cudaSuccess) return e;
     dim3 grid((unsigned)a.n_splits, (unsigned)a.NKV, (unsigned)a.n_qtiles);
-    fa_decode_kernel<HD, KVT><<<grid, kThreads, smem, st>>>(*tk, *tv, a);
-    return cudaGetLastError();
+    return launch_pdl_cluster(fa_decode_kernel<HD, KVT>, grid, dim3(kThreads), (size_t)smem, st,
+                              a.cluster_merge ? a.n_splits : 1, *tk, *tv, a);
+}
+
+// Largest cluster of this kernel the GPU can co-schedule (capped at 16); 1 if clusters are unusable.
+template <int HD, int KVT>
+int max_cluster_t() {
+    static int v = -1;
+    if (v < 0) {
+        using C = DecCfg<HD, KVT>;
+        if (prepare_t<HD, KVT>() != cudaSuccess) {
+            cudaGetLastError();
+            v = 1;
+            return v;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(16, 1, 1);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = C::SMEM + 1024;
+        int n = 0;
+        if (cudaOccupancyMaxPotentialClusterSize(&n, fa_decode_kernel<HD, KVT>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 1;
+        }
+        v = n < 1 ? 1 : (n > 16 ? 16 : n);
+    }
+    return v;
 }
 
 }  // namespace
+
+int decode_max_cluster(int head_dim, int kv_type) {
+    if (kv_type == SV_TYPE_Q8_0) return head_dim == 256 ? max_cluster_t<256, SV_TYPE_Q8_0>() : 1;
+    switch (head_dim) {
+        case 16: return max_cluster_t<16, SV_TYPE_F16>();
+        case 32: return max_cluster_t<32, SV_TYPE_F16>();
+        case 64: return max_cluster_t<64, SV_TYPE_F16>();
+        case 128: return max_cluster_t<128, SV_TYPE_F16>();
+        case 256: return max_cluster_t<256, SV_TYPE_F16>();
+        default: return 1;
+    }
+}
 
 int decode_block_keys() { return kBK; }
 

@@ -154,10 +154,6 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     const int qt = blockIdx.x, kvh = blockIdx.y;
     const int QPT = 128 / a.G;
     const int t0 = qt * QPT;
-    const int cbase = a.causal_base_dev ? __ldg(a.causal_base_dev) : a.causal_base;
-    const int nq = min(QPT, a.T - t0);
-    const int kend = min(a.S, cbase + t0 + nq);                 // keys [0, kend) reach some row
-    const int n_tiles = (kend + C::BN - 1) / C::BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::NS; s++) {
@@ -176,10 +172,20 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                      "r"((uint32_t)C::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    if (warp == 4 && lane == 0) {
+        tma_prefetch_desc(&tmk);
+        tma_prefetch_desc(&tmv);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();                      // everything above overlapped the previous kernel
+    if (threadIdx.x == 0) pdl_trigger();
+    const int cbase = a.causal_base_dev ? __ldg(a.causal_base_dev) : a.causal_base;
+    const int nq = min(QPT, a.T - t0);
+    const int kend = min(a.S, cbase + t0 + nq);                 // keys [0, kend) reach some row
+    const int n_tiles = (kend + C::BN - 1) / C::BN;
 
     if (warp < 4) {
         // ============================ softmax warps
@@ -302,8 +308,6 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     } else if (warp == 4) {
         // ============================ TMA producer
         if (lane == 0 && n_tiles > 0) {
-            tma_prefetch_desc(&tmk);
-            tma_prefetch_desc(&tmv);
             int issued = 0;
             for (int j = 0; j < n_tiles; j++) {
                 const int s = j % C::NS;
@@ -379,8 +383,7 @@ cudaError_t launch_t(const AttnArgs& a, const CUtensorMap* tk, const CUtensorMap
     }
     const int QPT = 128 / a.G;
     dim3 grid((unsigned)ceil_div(a.T, QPT), (unsigned)a.NKV);
-    fa_prefill_kernel<HD><<<grid, kPThreads, smem, st>>>(*tk, *tv, a);
-    return cudaGetLastError();
+    return launch_pdl(fa_prefill_kernel<HD>, grid, dim3(kPThreads), (size_t)smem, st, *tk, *tv, a);
 }
 
 }  // namespace

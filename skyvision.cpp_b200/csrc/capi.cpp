@@ -64,6 +64,7 @@ namespace {
 
 constexpr size_t kDefaultWsBytes = 64ull << 20;   // split-K partials per handle
 constexpr int kMaxTickets = 1 << 16;
+constexpr int kMaxSplits = 256;
 
 struct DeviceGuard {
     int prev = -1;
@@ -90,7 +91,7 @@ struct Plan {
 
 // span: keys one query tile may touch; ws_floats: capacity for partials
 Plan plan_decode(int T, int G, int NKV, int span, int head_dim, bool window, size_t ws_floats, int n_tickets,
-                 int target_ctas) {
+                 int target_ctas, int max_splits = kMaxSplits) {
     Plan p;
     const int BK = decode_block_keys();
     p.qpt = window ? 1 : std::max(1, 16 / G);
@@ -101,6 +102,10 @@ Plan plan_decode(int T, int G, int NKV, int span, int head_dim, bool window, siz
     auto set_splits = [&](int w) {
         p.chunk = std::max(BK, ceil_div(ceil_div(span, w), BK) * BK);
         p.n_splits = ceil_div(span, p.chunk);
+        if (p.n_splits > max_splits) {      // bounded merge tables in shared memory / cluster size
+            p.chunk = std::max(BK, ceil_div(ceil_div(span, max_splits), BK) * BK);
+            p.n_splits = ceil_div(span, p.chunk);
+        }
     };
     set_splits(want);
     const size_t per = decode_partial_floats(head_dim);
@@ -116,7 +121,15 @@ Plan plan_decode(int T, int G, int NKV, int span, int head_dim, bool window, siz
     return p;
 }
 
-int target_ctas_default() { return kNumSMs; }
+// CTAs the split plan aims for (SVKV_DEC_CTAS overrides it for tuning runs)
+int target_ctas_default() {
+    static const int v = [] {
+        const char* e = getenv("SVKV_DEC_CTAS");
+        const int n = e ? atoi(e) : 0;
+        return n > 0 ? n : kNumSMs;
+    }();
+    return v;
+}
 
 }  // namespace
 }  // namespace svkv
@@ -319,22 +332,40 @@ int sv_counter_add(int32_t* counter_dev, int delta, void* stream) {
 }
 
 // ------------------------------------------------------------------ attention
+static bool clusters_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("SVKV_CLUSTER");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* tv, const CUtensorMap* tkp,
                          const CUtensorMap* tvp, int head_dim, int kv_type, AttnArgs& a, int span, bool window,
-                         float* ws, size_t ws_bytes, int* tickets, int n_tickets, cudaStream_t st) {
+                         float* ws, size_t ws_bytes, int* tickets, int n_tickets, cudaStream_t st,
+                         bool allow_cluster = false) {
     (void)kvh;
     // chunked prefill on the tensor-core kernel when it applies
     if (!window && tkp && tvp && a.mask_mode == SV_MASK_CAUSAL && a.T * a.G > 16) {
         return cuda_status(launch_prefill(a, head_dim, tkp, tvp, st));
     }
     const size_t ws_floats = ws ? ws_bytes / sizeof(float) : 0;
-    Plan p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0,
-                         target_ctas_default());
+    // split-K merged inside a thread-block cluster (DSMEM) when the splits fit in one cluster
+    const int cmax = (allow_cluster && !window && clusters_enabled()) ? decode_max_cluster(head_dim, kv_type) : 1;
+    Plan p;
+    if (cmax >= 2) {
+        p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, (size_t)1 << 40, 1 << 30, target_ctas_default(), cmax);
+        a.cluster_merge = p.n_splits > 1;
+    } else {
+        p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0,
+                        target_ctas_default());
+        a.cluster_merge = 0;
+    }
     a.qpt = p.qpt;
     a.n_qtiles = p.n_qtiles;
     a.chunk = p.chunk;
     a.n_splits = p.n_splits;
-    if (a.n_splits > 1) {
+    if (a.n_splits > 1 && !a.cluster_merge) {
         const size_t n_part = (size_t)a.NKV * a.n_qtiles * a.n_splits * 16;
         a.ws_o = ws;
         a.ws_ml = ws + n_part * head_dim;
@@ -376,7 +407,7 @@ int sv_attn(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, 
     const CUtensorMap* tvp = kv->tm_pre.empty() ? nullptr : &kv->tm_pre[2 * layer + 1];
     return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], tkp, tvp, HD, kv->type, a,
                          n_past + T, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
-                         static_cast<cudaStream_t>(stream));
+                         static_cast<cudaStream_t>(stream), /*allow_cluster=*/true);
 }
 
 int sv_attn_at(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, const int32_t* n_past_dev,
@@ -411,7 +442,55 @@ int sv_attn_at(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_hea
     // the device-side base keeps the grid fixed: always the split-K decode kernel
     return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], nullptr, nullptr, HD, kv->type, a,
                          max_keys, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
-                         static_cast<cudaStream_t>(stream));
+                         static_cast<cudaStream_t>(stream), /*allow_cluster=*/true);
+}
+
+int sv_attn_append_at(sv_kv* kv, int layer, const void* q, int q_type, const void* k_new, const void* v_new, int T,
+                      int n_head, const int32_t* n_past_dev, int max_keys, float scale, float* out, void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !q || !out || !k_new || !v_new || T <= 0 || n_head <= 0 ||
+        !n_past_dev || max_keys < T)
+        return SV_ERR_INVALID;
+    if (n_head % kv->n_kv_head != 0 || n_head / kv->n_kv_head > 16) return SV_ERR_UNSUPPORTED;
+    const int G = n_head / kv->n_kv_head;
+    if (kv->type != SV_TYPE_F16 || T * G > 16) {
+        // the fused kernel covers f16 caches and one query tile; otherwise append, then attend
+        int rc = sv_kv_append_at(kv, layer, k_new, v_new, SV_TYPE_F16, T, n_past_dev, stream);
+        if (rc != SV_OK) return rc;
+        return sv_attn_at(kv, layer, q, q_type, T, n_head, n_past_dev, max_keys, scale, out, stream);
+    }
+    if (q_type != SV_TYPE_F16 && q_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if (max_keys > kv->n_ctx) return SV_ERR_OVERFLOW;
+    if (kv->tm_dec.empty()) return SV_ERR_UNSUPPORTED;
+    DeviceGuard g(kv->device);
+    const int HD = kv->head_dim;
+    const int es = q_type == SV_TYPE_F32 ? 4 : 2;
+    AttnArgs a{};
+    a.q = static_cast<const uint8_t*>(q);
+    a.q_type = q_type;
+    a.q_nb_h = (int64_t)HD * es;
+    a.q_nb_t = (int64_t)n_head * HD * es;
+    a.T = T;
+    a.NH = n_head;
+    a.NKV = kv->n_kv_head;
+    a.G = G;
+    a.S = max_keys;
+    a.mask_mode = SV_MASK_CAUSAL;
+    a.causal_base_dev = n_past_dev;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.out = out;
+    a.out_nb_h = HD;
+    a.out_nb_t = (int64_t)n_head * HD;
+    a.err = kv->err;
+    a.n_new = T;
+    a.knew = static_cast<const uint8_t*>(k_new);
+    a.vnew = static_cast<const uint8_t*>(v_new);
+    a.new_nb_t = (int64_t)kv->n_kv_head * HD * 2;
+    a.kc_w = kv->tensor(layer, 0);
+    a.vc_w = kv->tensor(layer, 1);
+    a.cache_row_bytes = kv->row_bytes;
+    return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], nullptr, nullptr, HD, kv->type, a,
+                         max_keys, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
+                         static_cast<cudaStream_t>(stream), /*allow_cluster=*/true);
 }
 
 int sv_attn_window(sv_kv* kv, int layer, const void* q, int q_type, int n_q, int n_head, const int32_t* lo,
@@ -446,7 +525,7 @@ int sv_attn_window(sv_kv* kv, int layer, const void* q, int q_type, int n_q, int
     a.err = kv->err;
     return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], nullptr, nullptr, HD, kv->type, a,
                          max_span + 1, true, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
-                         static_cast<cudaStream_t>(stream));
+                         static_cast<cudaStream_t>(stream), /*allow_cluster=*/true);
 }
 
 // ggml_flash_attn_ext with explicit views

@@ -49,12 +49,22 @@ struct AttnArgs {
     float scale_log2;       // scale * log2(e)
     int chunk;              // keys per split
     int n_splits;
+    int cluster_merge;      // 1: the n_splits CTAs of a tile form a cluster and merge through DSMEM
     float* out;             // (t, h, e) at out + t*out_nb_t + h*out_nb_h + e (floats)
     int64_t out_nb_t, out_nb_h;
     float* ws_o;            // split partials [tile][split][16][HD]
     float* ws_ml;           // [tile][split][16][2]
     int* tickets;           // [tile], zero between launches
     int* err;
+    // fused append (f16 cache, decode kernel): rows [cbase, cbase + n_new) come from knew/vnew
+    // (row stride new_nb_t bytes) and are written to kc_w/vc_w while being attended
+    int n_new;
+    const uint8_t* knew;
+    const uint8_t* vnew;
+    int64_t new_nb_t;
+    uint8_t* kc_w;
+    uint8_t* vc_w;
+    size_t cache_row_bytes;
 };
 
 struct PrefillArgs;  // attn_prefill.cu
@@ -92,6 +102,7 @@ bool decode_supported(int head_dim, int kv_type, size_t row_bytes, int n_kv_head
 bool make_decode_tmap(CUtensorMap* m, const void* base, int kv_type, int head_dim, int n_kv_head,
                       size_t row_bytes, int64_t n_rows);
 size_t decode_partial_floats(int head_dim);   // floats per (tile, split) partial incl. m/l
+int decode_max_cluster(int head_dim, int kv_type);   // largest co-schedulable cluster (<= 16), 1 = none
 int decode_block_keys();                       // BK
 cudaError_t launch_decode(const AttnArgs& a, int head_dim, int kv_type, const CUtensorMap* tk,
                           const CUtensorMap* tv, cudaStream_t st);

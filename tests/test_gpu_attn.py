@@ -251,10 +251,12 @@ def test_soft_max_ext(orc, ne0, rows):
 
 
 # ------------------------------------------------------------------ graph-capturable decode step
-def test_device_npast_graph_replay(orc):
-    """sv_kv_append_at + sv_attn_at + sv_counter_add captured once, replayed per token,
-    must equal the eager host-n_past path and the oracle."""
-    NKV, HD, NH, n0, steps = 8, 128, 32, 1000, 5
+@pytest.mark.parametrize("fused,NKV,HD,NH", [(False, 8, 128, 32), (True, 8, 128, 32), (True, 4, 256, 16),
+                                             (True, 2, 16, 8)])
+def test_device_npast_graph_replay(orc, fused, NKV, HD, NH):
+    """sv_kv_append_at + sv_attn_at (or the fused sv_attn_append_at) + sv_counter_add captured
+    once as a CUDA graph and replayed per token: cache rows bit-exact, attention vs the oracle."""
+    n0, steps = 1000, 5
     kv = sv.KvCache()
     assert kv.alloc(0, 2, NKV, HD, 2048)
     for layer in range(2):
@@ -272,8 +274,12 @@ def test_device_npast_graph_replay(orc):
 
     def step():
         for layer in range(2):
-            kv.append_at(layer, dk[layer], dv[layer], npast, stream=st)
-            kv.attn_at(layer, dq[layer], npast, max_keys, 1 / np.sqrt(HD), out=dout[layer], stream=st)
+            if fused:
+                kv.attn_append_at(layer, dq[layer], dk[layer], dv[layer], npast, max_keys, 1 / np.sqrt(HD),
+                                  out=dout[layer], stream=st)
+            else:
+                kv.append_at(layer, dk[layer], dv[layer], npast, stream=st)
+                kv.attn_at(layer, dq[layer], npast, max_keys, 1 / np.sqrt(HD), out=dout[layer], stream=st)
         sv.counter_add(npast, 1, stream=st)
 
     with torch.cuda.stream(st):
