@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="svkv", choices=["svkv", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the config-5 multi-session leg")
     return ap.parse_args()
 
 
@@ -410,6 +411,9 @@ def run_svkv(args, world, rank, local):
     prefill_ms_max = max_over_ranks(prefill_ms, world)
     clocks = clk.summary()
     kv.free()
+    del kv
+    torch.cuda.empty_cache()
+    batched = None if args.no_batched else run_batched(sv, dev, stream, rank, world, K, W)
     if rank != 0:
         return
 
@@ -462,6 +466,8 @@ def run_svkv(args, world, rank, local):
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if batched is not None:
+        line["batched"] = batched
     if world == 1 and not args.no_cpu_baseline:
         n_layers, n_tok = 8, 12
         per_tl, cores = cpu_decode_sample(n_layers, n_tok)
@@ -470,6 +476,122 @@ def run_svkv(args, world, rank, local):
             "sample": f"{n_tok} decode tokens through {n_layers} of 36 layers (S~4481), per-token time x{L / n_layers:g}",
         }
     print(json.dumps(line), flush=True)
+
+
+def cfg5_shards(n_gpus: int = 8):
+    """64 session lengths U[512, 32768] (numpy default_rng(4)), balanced over
+    n_gpus by longest-first greedy assignment on total context."""
+    lens = np.random.default_rng(4).integers(512, 32769, 64)
+    order = np.argsort(-lens, kind="stable")
+    loads = [0] * n_gpus
+    shards = [[] for _ in range(n_gpus)]
+    for i in order:
+        g = int(np.argmin(loads))
+        shards[g].append(int(i))
+        loads[g] += int(lens[i])
+    return lens, shards
+
+
+def run_batched(sv, dev, stream, rank, world, K, W):
+    """Config-5 multi-session decode: this GPU's eighth of the 64 sessions (8 sessions, ~150k cached
+    rows, ~22 GB of K/V over 36 layers) in one shared cache with per-session slot ranges; each step
+    appends one row per session and runs the windowed attention for all sessions per layer
+    (vc3_batch.inc's batched step), captured once as a CUDA graph.  Weak scaling: every rank serves
+    its own shard (rank r takes shard r mod 8)."""
+    import torch
+    lens, shards = cfg5_shards(8)
+    mine = shards[rank % 8]
+    ctx = [int(lens[i]) for i in mine]
+    n = len(ctx)
+    room = K + W + 64
+    caps = [c + room for c in ctx]
+    base = np.concatenate([[0], np.cumsum(caps)[:-1]]).astype(np.int32)
+    n_ctx = int(sum(caps))
+    kv = sv.KvCache()
+    if not kv.alloc(dev.index, L, NKV, HD, n_ctx):
+        raise SystemExit("KvCache.alloc failed (config 5 shard)")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4000 + rank)
+    with torch.cuda.stream(stream):
+        for layer in range(L):
+            for isv in (0, 1):
+                kv.tensor(layer, isv).view(torch.float16).normal_(generator=gen)
+        lo = torch.tensor(base, dtype=torch.int32, device=dev)
+        own0 = lo + torch.tensor(ctx, dtype=torch.int32, device=dev)
+        own = own0.clone()
+        hi = own + 1
+        q = torch.randn(L, n, NH, HD, generator=gen, device=dev).half()
+        knew = torch.randn(L, n, NKV * HD, generator=gen, device=dev).half()
+        vnew = torch.randn(L, n, NKV * HD, generator=gen, device=dev).half()
+        out = torch.empty(L, n, NH, HD, dtype=torch.float32, device=dev)
+        max_span = max(ctx) + room
+
+        def reset():
+            own.copy_(own0)
+            hi.copy_(own0 + 1)
+
+        def step():
+            for layer in range(L):
+                kv.append(layer, knew[layer], vnew[layer], rows=own, stream=stream)
+                kv.attn_window(layer, q[layer], lo, hi, own, max_span, SCALE, out=out[layer], stream=stream)
+            sv.counter_add(hi, 1, stream=stream)
+            sv.counter_add(own, 1, stream=stream)
+
+        step()
+        stream.synchronize()
+        reset()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        for _ in range(W):
+            g.replay()
+        reset()
+        stream.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(K):
+            g.replay()
+        e1.record(stream)
+        e1.synchronize()
+        barrier(world)
+        ms = e0.elapsed_time(e1)
+        assert kv.error_flags(stream=stream) == 0
+        # the windowed attention kernel alone (36 launches per replay) at the middle step
+        own.copy_(own0 + K // 2)
+        hi.copy_(own + 1)
+        ga = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(ga, stream=stream):
+            for layer in range(L):
+                kv.attn_window(layer, q[layer], lo, hi, own, max_span, SCALE, out=out[layer], stream=stream)
+        ga.replay()
+        stream.synchronize()
+        ra = 5
+        e0.record(stream)
+        for _ in range(ra):
+            ga.replay()
+        e1.record(stream)
+        e1.synchronize()
+        attn_ms = e0.elapsed_time(e1) / (ra * L)
+    ms_max = max_over_ranks(ms, world)
+    kv.free()
+    row_b = NKV * HD * 2 * 2                     # K + V bytes of one cached row
+    step_bytes = sum(L * ((c + i + 1) * row_b + NH * HD * 6) for c in ctx for i in range(K)) / K + L * n * append_bytes(1)
+    attn_bytes = sum((c + K // 2 + 1) * row_b + NH * HD * 6 for c in ctx)
+    hbm, _, peak_kind = measured_peaks()
+    return {
+        "workload": f"BASELINE config 5 shard: {n} of 64 sessions per GPU (ctx {min(ctx)}..{max(ctx)}, "
+                    f"sum {sum(ctx)}), 36 layers, 32q/8kv HD 128 f16, one shared cache with slot ranges",
+        "tokens_per_s": world * n * K / (ms_max * 1e-3),
+        "ms_per_step": ms_max / K,
+        "kv_gbs": world * step_bytes / (ms_max / K * 1e-3) / 1e9,
+        "roofline": {"kernel": "fa_decode_kernel<128, f16> window mode (sv_attn_window)", "bound": "hbm",
+                     "achieved": attn_bytes / (attn_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": attn_bytes / (attn_ms * 1e-3) / 1e9 / hbm,
+                     "peak_source": f"{peak_kind} hbm_gbs", "bytes_per_launch": attn_bytes,
+                     "launch_us": attn_ms * 1e3},
+        "gpu_launches": K * (2 * L + 2),
+    }
 
 
 def main():

@@ -128,8 +128,9 @@ int sv_kv_append(sv_kv* kv, int layer, const void* k, const void* v, int src_typ
 int sv_kv_append_at(sv_kv* kv, int layer, const void* k, const void* v, int src_type, int n_rows,
                     const int32_t* base_dev, void* stream);
 
-/* *counter_dev += delta on the stream (advances the device-side n_past). */
-int sv_counter_add(int32_t* counter_dev, int delta, void* stream);
+/* counter_dev[i] += delta for i < n, on the stream (advances device-side n_past
+ * values / per-session window ends between replays of a captured step). */
+int sv_counter_add(int32_t* counter_dev, int n, int delta, void* stream);
 
 /* ================================================================ attention
  * ggml_flash_attn_ext(q, k, v, mask, scale, max_bias = 0, softcap = 0)

@@ -95,7 +95,7 @@ def lib() -> ctypes.CDLL:
         "sv_set_rows": (I, [P, I, I64, I64, SZ, P, I, SZ, I64, P, I64, P, P]),
         "sv_kv_append": (I, [P, I, P, P, I, I, P, I, P]),
         "sv_kv_append_at": (I, [P, I, P, P, I, I, P, P]),
-        "sv_counter_add": (I, [P, I, P]),
+        "sv_counter_add": (I, [P, I, I, P]),
         "sv_attn_at": (I, [P, I, P, I, I, I, P, I, F, P, P]),
         "sv_attn_append_at": (I, [P, I, P, I, P, P, I, I, P, I, F, P, P]),
         "sv_flash_attn_ext_workspace": (SZ, [ctypes.POINTER(_FaParams)]),
@@ -279,8 +279,8 @@ class KvCache:
 
 
 def counter_add(counter, delta: int, stream=None) -> None:
-    """counter (int32 device tensor [1]) += delta, on the stream."""
-    _check("sv_counter_add", lib().sv_counter_add(_ptr(counter), delta, _stream(stream)))
+    """counter (int32 device tensor [n]) += delta elementwise, on the stream."""
+    _check("sv_counter_add", lib().sv_counter_add(_ptr(counter), counter.numel(), delta, _stream(stream)))
 
 
 # =================================================================== ggml-op forms

@@ -159,16 +159,17 @@ set_rows_kernel(uint8_t* __restrict__ dst, int dst_type, int64_t ne0, int64_t ds
     }
 }
 
-__global__ void counter_add_kernel(int32_t* c, int delta) {
+__global__ void counter_add_kernel(int32_t* c, int n, int delta) {
     pdl_wait();
-    *c += delta;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) c[i] += delta;
     pdl_trigger();
 }
 
 }  // namespace
 
-cudaError_t launch_counter_add(int32_t* counter, int delta, cudaStream_t st) {
-    return launch_pdl(counter_add_kernel, dim3(1), dim3(1), 0, st, counter, delta);
+cudaError_t launch_counter_add(int32_t* counter, int n, int delta, cudaStream_t st) {
+    return launch_pdl(counter_add_kernel, dim3(1), dim3(n < 256 ? ((n + 31) / 32) * 32 : 256), 0, st, counter, n,
+                      delta);
 }
 
 cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,

@@ -326,9 +326,9 @@ int sv_kv_append_at(sv_kv* kv, int layer, const void* k, const void* v, int src_
     return cuda_status(e);
 }
 
-int sv_counter_add(int32_t* counter_dev, int delta, void* stream) {
-    if (!counter_dev) return SV_ERR_INVALID;
-    return cuda_status(launch_counter_add(counter_dev, delta, static_cast<cudaStream_t>(stream)));
+int sv_counter_add(int32_t* counter_dev, int n, int delta, void* stream) {
+    if (!counter_dev || n <= 0) return SV_ERR_INVALID;
+    return cuda_status(launch_counter_add(counter_dev, n, delta, static_cast<cudaStream_t>(stream)));
 }
 
 // ------------------------------------------------------------------ attention
@@ -357,8 +357,10 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
         p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, (size_t)1 << 40, 1 << 30, target_ctas_default(), cmax);
         a.cluster_merge = p.n_splits > 1;
     } else {
-        p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0,
-                        target_ctas_default());
+        // per-query windows differ in length (multi-session batches): aim for several waves of
+        // CTAs so the short sessions' idle splits do not leave SMs waiting on the long ones
+        const int target = window ? 8 * target_ctas_default() : target_ctas_default();
+        p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0, target);
         a.cluster_merge = 0;
     }
     a.qpt = p.qpt;

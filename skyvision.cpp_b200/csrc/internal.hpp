@@ -120,7 +120,7 @@ cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_ro
                             size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st,
                             const int32_t* base_dev = nullptr);
 
-cudaError_t launch_counter_add(int32_t* counter, int delta, cudaStream_t st);
+cudaError_t launch_counter_add(int32_t* counter, int n, int delta, cudaStream_t st);
 
 cudaError_t launch_compact(KvHandle* kv, const int32_t* seg_dev_unused, const sv_segment* segs, int n_segs,
                            int dst_base, cudaStream_t st);

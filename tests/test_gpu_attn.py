@@ -236,6 +236,67 @@ def test_window_multi_session(orc):
     close(out.cpu().numpy(), ref)
 
 
+def test_window_batch_graph_replay(orc):
+    """Batched multi-session decode as the bench runs it: per step and layer, set_rows of one new row
+    per session at its own slot, windowed attention per session, then advance the windows on the
+    device; captured once as a CUDA graph and replayed."""
+    NKV, HD, NH, steps = 8, 128, 32, 3
+    ctx = [70, 1500, 5, 900]
+    caps = [c + 16 for c in ctx]
+    base = np.concatenate([[0], np.cumsum(caps)[:-1]]).astype(np.int32)
+    n = len(ctx)
+    kv = sv.KvCache()
+    assert kv.alloc(0, 2, NKV, HD, int(sum(caps)))
+    for layer in range(2):
+        fill_cache(orc, kv, layer, int(sum(caps)), seed=20 + layer)
+    td = lambda a: torch.from_numpy(a).to(DEV)
+    lo = td(base)
+    own0 = td(base + np.array(ctx, np.int32))
+    own = own0.clone()
+    hi = own + 1
+    ne0 = NKV * HD
+    q = [orc.normal_f16(21, 10 + i, 2 * n * NH * HD).reshape(2, n, NH, HD) for i in range(steps)]
+    k = [orc.normal_f16(21, 40 + i, 2 * n * ne0).reshape(2, n, ne0) for i in range(steps)]
+    v = [orc.normal_f16(21, 70 + i, 2 * n * ne0).reshape(2, n, ne0) for i in range(steps)]
+    dq, dk, dv = td(q[0].view(np.float16)).clone(), td(k[0].view(np.float16)).clone(), td(v[0].view(np.float16)).clone()
+    out = torch.zeros(2, n, NH, HD, dtype=torch.float32, device=DEV)
+    st = torch.cuda.Stream()
+    max_span = max(ctx) + steps + 2
+
+    def step():
+        for layer in range(2):
+            kv.append(layer, dk[layer], dv[layer], rows=own, stream=st)
+            kv.attn_window(layer, dq[layer], lo, hi, own, max_span, 1 / np.sqrt(HD), out=out[layer], stream=st)
+        sv.counter_add(hi, 1, stream=st)
+        sv.counter_add(own, 1, stream=st)
+
+    with torch.cuda.stream(st):
+        g = torch.cuda.CUDAGraph()
+        step()                      # eager run (kernel attributes), then rewind the windows
+        st.synchronize()
+        own.copy_(own0)
+        hi.copy_(own0 + 1)
+        with torch.cuda.graph(g, stream=st):
+            step()
+        for i in range(steps):
+            dq.copy_(td(q[i].view(np.float16)))
+            dk.copy_(td(k[i].view(np.float16)))
+            dv.copy_(td(v[i].view(np.float16)))
+            g.replay()
+            st.synchronize()
+            got = out.cpu().numpy()
+            own_h = base + np.array(ctx, np.int32) + i
+            for layer in range(2):
+                kc = kv.tensor(layer, 0).cpu().numpy()
+                vc = kv.tensor(layer, 1).cpu().numpy()
+                for s in range(n):
+                    assert np.array_equal(kc[own_h[s]].view(np.uint16), k[i][layer, s])
+                ref = orc.attn(orc.f16_to_f32(q[i][layer]), kc, vc, orc.TYPE_F16, NKV, HD, kc.shape[0],
+                               1 / np.sqrt(HD), orc.MASK_WINDOW, lo=base, hi=own_h + 1, own=own_h)
+                close(got[layer], ref)
+    assert kv.error_flags() == 0
+
+
 # ------------------------------------------------------------------ soft_max fallback
 @pytest.mark.parametrize("ne0,rows", [(1088, 32), (33, 5), (4096, 3)])
 def test_soft_max_ext(orc, ne0, rows):
