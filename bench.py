@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", default="svkv", choices=["svkv", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-5 multi-session leg")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx"],
+                    help="cfg2: the headline line; longctx: one 131072-token session sharded by kv head")
     return ap.parse_args()
 
 
@@ -594,6 +596,102 @@ def run_batched(sv, dev, stream, rank, world, K, W):
     }
 
 
+def run_longctx(args, world, rank, local):
+    """One 131072-token session (config-5 long-context run) sharded by KV head: rank g keeps kv heads
+    [g*8/G, (g+1)*8/G) of all 36 layers and their query heads; per layer the fused append + attention
+    kernel runs on the local heads, then NCCL all-gathers the head outputs over NVLink.  Strong
+    scaling: the session's work is fixed, value = decode tokens/s of that session."""
+    import importlib
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    sv = load_package()
+    sh = importlib.import_module("skyvision_b200.sharding")
+    dev = torch.device(f"cuda:{local}")
+    stream = torch.cuda.Stream(device=dev)
+    K, W = args.steps, args.warmup
+    S0 = 131072
+    hs = sh.HeadShardedDecode(NH, NKV, HD, rank, world)
+    nkv_l, nh_l = hs.kv_hi - hs.kv_lo, hs.q_hi - hs.q_lo
+    kv = sv.KvCache()
+    if not kv.alloc(local, L, nkv_l, HD, S0 + K + W + 64):
+        raise SystemExit("KvCache.alloc failed (long context)")
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5000 + rank)
+    with torch.cuda.stream(stream):
+        for layer in range(L):
+            for isv in (0, 1):
+                kv.tensor(layer, isv).view(torch.float16).normal_(generator=gen)
+        npast = torch.full((1,), S0, dtype=torch.int32, device=dev)
+        ql = torch.randn(L, 1, nh_l, HD, generator=gen, device=dev).half()
+        kl = torch.randn(L, 1, nkv_l * HD, generator=gen, device=dev).half()
+        vl = torch.randn(L, 1, nkv_l * HD, generator=gen, device=dev).half()
+        out_l = torch.empty(L, 1, nh_l, HD, dtype=torch.float32, device=dev)
+        out_f = torch.empty(L, 1, NH, HD, dtype=torch.float32, device=dev)
+        max_keys = S0 + K + W + 1
+
+        def step():
+            for layer in range(L):
+                kv.attn_append_at(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE, out=out_l[layer],
+                                  stream=stream)
+                hs.gather(out_l[layer], out_f[layer])
+            sv.counter_add(npast, 1, stream=stream)
+
+        step()
+        stream.synchronize()
+        npast.fill_(S0)
+        g = None
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step()
+            run = g.replay
+            how = "one CUDA graph per step (attention kernels + NCCL all-gathers)"
+        except Exception as ex:         # capture of the collective unavailable: eager steps
+            g = None
+            torch.cuda.synchronize()
+            run = step
+            how = f"eager steps (graph capture failed: {type(ex).__name__})"
+        for _ in range(W):
+            run()
+        npast.fill_(S0)
+        stream.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(K):
+                run()
+            e1.record(stream)
+            e1.synchronize()
+        barrier(world)
+        ms = e0.elapsed_time(e1)
+        assert kv.error_flags(stream=stream) == 0
+    ms_max = max_over_ranks(ms, world)
+    del g
+    kv.free()
+    if rank != 0:
+        return
+    row_b = NKV * HD * 2 * 2
+    step_bytes = sum(L * ((S0 + i + 1) * row_b + NH * HD * 6) for i in range(K)) / K
+    hbm, _, peak_kind = measured_peaks()
+    line = {
+        "metric": "decode attn tokens/s, one 131072-token session sharded by kv head",
+        "value": K / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "one session of 131072 cached rows, 36 layers, 32q/8kv HD 128 f16 "
+                               f"({nkv_l} kv heads per GPU)", "step": how,
+                   "parallelism": f"kv-head sharding over {world} GPU(s), NCCL all-gather of head outputs per layer"},
+        "kv_gbs": step_bytes / (ms_max / K * 1e-3) / 1e9,
+        "kv_gbs_per_gpu": step_bytes / world / (ms_max / K * 1e-3) / 1e9,
+        "hbm_frac_per_gpu": step_bytes / world / (ms_max / K * 1e-3) / 1e9 / hbm,
+        "gpu_launches": K * (L + 1),
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world, rank, local = (1, 0, 0)
@@ -604,7 +702,10 @@ def main():
         return
     world, rank, local = dist_setup(args)
     try:
-        run_svkv(args, world, rank, local)
+        if args.workload == "longctx":
+            run_longctx(args, world, rank, local)
+        else:
+            run_svkv(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

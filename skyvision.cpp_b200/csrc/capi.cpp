@@ -353,8 +353,14 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     // split-K merged inside a thread-block cluster (DSMEM) when the splits fit in one cluster
     const int cmax = (allow_cluster && !window && clusters_enabled()) ? decode_max_cluster(head_dim, kv_type) : 1;
     Plan p;
+    bool use_cluster = false;
     if (cmax >= 2) {
         p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, (size_t)1 << 40, 1 << 30, target_ctas_default(), cmax);
+        // a cluster caps the splits of a tile; when that leaves most SMs idle (few kv heads and a
+        // long context, e.g. one kv head per GPU), the ticket merge with more splits wins
+        use_cluster = (size_t)a.NKV * p.n_qtiles * p.n_splits * 2 >= (size_t)target_ctas_default();
+    }
+    if (use_cluster) {
         a.cluster_merge = p.n_splits > 1;
     } else {
         // per-query windows differ in length (multi-session batches): aim for several waves of
