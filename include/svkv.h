@@ -266,6 +266,16 @@ int sv_session_end_turn(sv_session* s, int frames, int text_rows, int answer_row
  * compacted) row id of cache row i, i < *n_rows (max_rows caps the copy). */
 int sv_session_rows(const sv_session* s, int* n_rows, int64_t* rows_out, int max_rows);
 
+/* ================================================================ failure detection
+ * Every on-device wait of the library is bounded; on expiry the kernel sets
+ * SV_DEVERR_TIMEOUT in its error word and unwinds instead of hanging.  This
+ * self-test runs a one-warp kernel whose wait can never complete, with a limit
+ * of limit_us microseconds (<= 1 s): afterwards *err_dev has SV_DEVERR_TIMEOUT
+ * set and *reached_end_dev (may be NULL) is 1 (the kernel returned past the
+ * expired wait).  The reference has no device-side failure detection (errors
+ * are bool returns, src/core/engine/attention.hpp:38-42, qwen3vl_model.cpp:743). */
+int sv_selftest_wait_timeout(int* err_dev, int* reached_end_dev, unsigned limit_us, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -111,6 +111,7 @@ def lib() -> ctypes.CDLL:
         "sv_session_begin_turn": (I, [P, I, ctypes.POINTER(I), ctypes.POINTER(I), P]),
         "sv_session_end_turn": (I, [P, I, I, I]),
         "sv_session_rows": (I, [P, ctypes.POINTER(I), P, I]),
+        "sv_selftest_wait_timeout": (I, [P, P, ctypes.c_uint, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
