@@ -53,8 +53,9 @@ def parse():
     ap.add_argument("--impl", default="svkv", choices=["svkv", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-5 multi-session leg")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx"],
-                    help="cfg2: the headline line; longctx: one 131072-token session sharded by kv head")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx", "kernels"],
+                    help="cfg2: the headline line; longctx: one 131072-token session sharded by kv head; "
+                         "kernels: one small launch set of every kernel (for ncu captures)")
     return ap.parse_args()
 
 
@@ -750,6 +751,68 @@ def run_cfg4(sv, dev, stream):
     }
 
 
+def run_kernels(args):
+    """Each kernel of the path on a small single-layer case, 3 launches each in this order:
+    fused decode (config 2 geometry, S = 4481), windowed decode (2 sessions of ~19k rows),
+    chunked prefill (384 over 4096), f16 and q8_0 append, compaction, q8_0 decode (config 4
+    geometry).  Under 1 GB on the device; used by the committed ncu summaries."""
+    import torch
+    from __graft_entry__ import load_package
+    sv = load_package()
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    times = {}
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+
+    def timed(name, fn, reps=3):
+        fn()
+        torch.cuda.synchronize()
+        a, b = ev(), ev()
+        a.record()
+        for _ in range(reps - 1):
+            fn()
+        b.record()
+        b.synchronize()
+        times[name] = a.elapsed_time(b) / max(reps - 1, 1) * 1e3
+
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, NKV, HD, 8192)
+    kv.tensor(0, 0).view(torch.float16).normal_(generator=g)
+    kv.tensor(0, 1).view(torch.float16).normal_(generator=g)
+    npast = torch.full((1,), PRE + TAIL, dtype=torch.int32, device=dev)
+    q1 = torch.randn(1, NH, HD, generator=g, device=dev).half()
+    k1 = torch.randn(1, NKV * HD, generator=g, device=dev).half()
+    timed("decode_fused_us", lambda: kv.attn_append_at(0, q1, k1, k1, npast, PRE + TAIL + 8, SCALE))
+    kw = sv.KvCache()
+    assert kw.alloc(0, 1, NKV, HD, 40000)
+    kw.tensor(0, 0).view(torch.float16).normal_(generator=g)
+    kw.tensor(0, 1).view(torch.float16).normal_(generator=g)
+    lo = torch.tensor([0, 20000], dtype=torch.int32, device=dev)
+    own = torch.tensor([18000, 39000], dtype=torch.int32, device=dev)
+    hi = own + 1
+    q2 = torch.randn(2, NH, HD, generator=g, device=dev).half()
+    timed("decode_window_us", lambda: kw.attn_window(0, q2, lo, hi, own, 19001, SCALE))
+    qt = torch.randn(TAIL, NH, HD, generator=g, device=dev).half()
+    timed("prefill_us", lambda: kv.attn(0, qt, n_past=PRE, scale=SCALE))
+    kt = torch.randn(TAIL, NKV * HD, generator=g, device=dev).half()
+    timed("append_f16_us", lambda: kv.append(0, kt, kt, base=PRE))
+    kq = sv.KvCache()
+    assert kq.alloc(0, 1, 4, 256, 8192 + 64, sv.TYPE_Q8_0)
+    kt4 = torch.randn(512, 1024, generator=g, device=dev).half()
+    timed("append_q8_0_us", lambda: kq.append(0, kt4, kt4, base=0))
+    segs = [(0, 1152, 0), (1152, 5 * 1152, 1)]
+    timed("compact_us", lambda: kv.compact(segs, 0))
+    for c in range(16):
+        kq.append(0, kt4, kt4, base=c * 512)
+    npq = torch.full((1,), 8192, dtype=torch.int32, device=dev)
+    q4 = torch.randn(1, 16, 256, generator=g, device=dev).half()
+    timed("decode_q8_0_us", lambda: kq.attn_at(0, q4, npq, 8193, 1 / 16.0))
+    torch.cuda.synchronize()
+    assert kv.error_flags() == 0 and kq.error_flags() == 0 and kw.error_flags() == 0
+    print(json.dumps({"workload": "kernels", "us_per_launch": times}), flush=True)
+
+
 def run_longctx(args, world, rank, local):
     """One 131072-token session (config-5 long-context run) sharded by KV head: rank g keeps kv heads
     [g*8/G, (g+1)*8/G) of all 36 layers and their query heads; per layer the fused append + attention
@@ -853,6 +916,9 @@ def main():
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, world, rank)
+        return
+    if args.workload == "kernels":
+        run_kernels(args)
         return
     world, rank, local = dist_setup(args)
     try:
