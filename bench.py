@@ -356,7 +356,7 @@ def run_svkv(args, world, rank, local):
         dec_ms = e0.elapsed_time(e1)
         launches = K * (L + 1)
         assert int(npast.item()) == n0 + K
-        assert kv.error_flags(stream=stream) == 0
+        check_flags(kv, stream)
         S_steps = [n0 + i + 1 for i in range(K)]
         step_bytes = sum(L * (decode_attn_bytes(S) + append_bytes(1)) for S in S_steps) / K
 
@@ -459,7 +459,7 @@ def run_svkv(args, world, rank, local):
             "frac_of_bf16_peak": prefill_tflops / tflops_peak,
         },
         "roofline": {
-            "kernel": "fa_decode_kernel<128, f16> fused append + attention (sv_attn_append_at)",
+            "kernel": "fa_decode_gqa_kernel<128> fused append + attention (sv_attn_append_at)",
             "bound": "hbm",
             "achieved": attn_gbs,
             "peak": hbm,
@@ -567,7 +567,7 @@ def run_batched(sv, dev, stream, rank, world, K, W):
         e1.synchronize()
         barrier(world)
         ms = e0.elapsed_time(e1)
-        assert kv.error_flags(stream=stream) == 0
+        check_flags(kv, stream)
         # the windowed attention kernel alone (36 launches per replay) at the middle step
         own.copy_(own0 + K // 2)
         hi.copy_(own + 1)
@@ -663,7 +663,7 @@ def run_cfg3(sv, dev, stream):
             sess.end_turn(kept, text, answer)
             ref.end_turn(kept, text, answer)
         assert np.array_equal(sess.rows(), ref.rows()), "kept-row set differs from the window rule"
-        assert kv.error_flags(stream=stream) == 0
+        check_flags(kv, stream)
     kv.free()
     return {
         "workload": "BASELINE config 3: 12 rounds x (16 frames x 64 rows + 96 text + 32 answer rows), window 6 "
@@ -735,7 +735,7 @@ def run_cfg4(sv, dev, stream):
         e1.record(stream)
         e1.synchronize()
         dec_ms = e0.elapsed_time(e1)
-        assert kv.error_flags(stream=stream) == 0
+        check_flags(kv, stream)
     del g
     kv.free()
     headb = HDq // 32 * 34
@@ -749,6 +749,12 @@ def run_cfg4(sv, dev, stream):
         "decode_tokens_per_s": DEC4 / (dec_ms * 1e-3),
         "decode_kv_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9,
     }
+
+
+def check_flags(kv, stream=None):
+    """Device error bits of a cache handle (row range, expired wait, bad segment) must be clear."""
+    f = kv.error_flags(stream=stream)
+    assert f == 0, f"device error bits 0x{f:x}"
 
 
 def run_kernels(args):
@@ -883,7 +889,7 @@ def run_longctx(args, world, rank, local):
             e1.synchronize()
         barrier(world)
         ms = e0.elapsed_time(e1)
-        assert kv.error_flags(stream=stream) == 0
+        check_flags(kv, stream)
     ms_max = max_over_ranks(ms, world)
     del g
     kv.free()

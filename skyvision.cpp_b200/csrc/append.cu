@@ -52,10 +52,14 @@ __global__ void __launch_bounds__(kAppendThreads)
 set_rows_kernel(uint8_t* __restrict__ dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
                 const uint8_t* __restrict__ src, int src_type, size_t src_nb1,
                 const int32_t* __restrict__ rows, int64_t base, int* err,
-                size_t dst_tensor_stride, size_t src_tensor_stride, const int32_t* __restrict__ base_dev) {
+                size_t dst_tensor_stride, size_t src_tensor_stride, const int32_t* __restrict__ base_dev,
+                int early_trigger) {
     extern __shared__ __align__(16) uint8_t qrow[];   // q8_0 row staging
     pdl_wait();
-    if (threadIdx.x == 0) pdl_trigger();
+    // Letting the next launch start early is safe only when the host knows it will not read cache
+    // rows before its own grid dependency resolves (cache handles track that; see run_attention);
+    // otherwise dependents start when every row of this launch is written.
+    if (early_trigger && threadIdx.x == 0) pdl_trigger();
     const int64_t i = blockIdx.x;
     const int z = blockIdx.y;
     const int64_t r = rows ? (int64_t)rows[i] : (base_dev ? (int64_t)__ldg(base_dev) : base) + i;
@@ -176,7 +180,7 @@ cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_ro
                             const void* src, int src_type, size_t src_nb1, int64_t n_rows,
                             const int32_t* rows, int64_t base, int* err, int n_tensors,
                             size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st,
-                            const int32_t* base_dev) {
+                            const int32_t* base_dev, bool early_trigger) {
     if (n_rows <= 0) return cudaSuccess;
     const size_t smem = dst_type == SV_TYPE_Q8_0 ? row_bytes_of(SV_TYPE_Q8_0, ne0) : 0;
     if (smem > 48 * 1024) {
@@ -187,7 +191,7 @@ cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_ro
     dim3 grid((unsigned)n_rows, (unsigned)n_tensors);
     return launch_pdl(set_rows_kernel, grid, dim3(kAppendThreads), smem, st, static_cast<uint8_t*>(dst), dst_type, ne0,
                       dst_rows, dst_nb1, static_cast<const uint8_t*>(src), src_type, src_nb1, rows, base, err,
-                      dst_tensor_stride, src_tensor_stride, base_dev);
+                      dst_tensor_stride, src_tensor_stride, base_dev, early_trigger ? 1 : 0);
 }
 
 }  // namespace svkv

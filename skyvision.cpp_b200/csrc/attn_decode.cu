@@ -134,10 +134,11 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     };
     // A kernel that appends its own new rows (fused decode step) starts streaming its split's
     // first tiles before waiting for the previous kernel: the rows it reads were completed by
-    // earlier steps, and the rows it appends are patched in from their source below.  The
-    // split's start does not depend on n_past in causal mode, only its end does.
+    // earlier steps (the host clears ring_prefill when the launch before this one wrote cache rows
+    // while letting it start early), and the rows it appends are patched in from their source
+    // below.  The split's start does not depend on n_past in causal mode, only its end does.
     int prefetched = 0;
-    if (a.n_new > 0 && a.mask_mode == SV_MASK_CAUSAL && threadIdx.x == kConsumerWarps * 32) {
+    if (a.n_new > 0 && a.ring_prefill && a.mask_mode == SV_MASK_CAUSAL && threadIdx.x == kConsumerWarps * 32) {
         const int ks0 = split * a.chunk;
         const int kmax = min(a.S, ks0 + a.chunk);
         const int nt_max = kmax > ks0 ? (kmax - ks0 + kBK - 1) / kBK : 0;

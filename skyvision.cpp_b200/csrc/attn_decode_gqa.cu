@@ -1,0 +1,589 @@
+// attn_decode_gqa.cu - single-step decode attention over an f16 KV cache for
+// grouped-query heads (sm_100a): the latency-critical form of
+// ggml_flash_attn_ext at T * (NH/NKV) <= 8 query rows per kv head
+// (llm_block.hpp:268-277, qwen3vl_model.cpp:657-663 with T = 1), causal or
+// unmasked.
+//
+// Why a second decode kernel.  With one token and 4 query heads per kv head a
+// 16-row MMA tile is 75 % empty when queries are the M dimension, and the
+// per-tile MMA chain (not HBM) bounds each split.  Here keys are the M
+// dimension and the query rows the N dimension ("swap AB"):
+//   S^T(16 keys x 8 rows)  = K(16 x HD) * Q^T(HD x 8)       mma.m16n8k16, K by ldmatrix
+//   O^T(HD x 8 rows)      += V^T(HD x 16 keys) * P^T(16 x 8)  V by ldmatrix.trans,
+//                                                          P^T by movmatrix.trans
+// which halves the MMAs per key, keeps O in 32 registers per thread and lets
+// two groups of four consumer warps work on alternate K/V tiles while two CTAs
+// share an SM.  Each warp owns 16 keys of every 64-key tile of its group.
+//
+// Latency path (a decode step is a chain of one launch per layer): before the
+// programmatic grid-dependency wait the kernel only issues loads that no
+// earlier kernel of the step can change: L2 prefetches of the query rows and of
+// every K/V tile of the split past the shared-memory ring, and - when the
+// kernel appends the step's row itself - TMA fills of the ring.  The next
+// launch may start once every split has issued its last tile.  The split-K
+// partials of a kv head merge inside a thread-block cluster: CTA 0 of the
+// cluster does no K/V work; every split pushes its partial into CTA 0's shared
+// memory with st.async (completion counted on CTA 0's mbarrier) and exits, and
+// CTA 0 merges and stores, so no split waits on a cluster-wide barrier.
+// Measured on config 2 (36 layers, S ~ 4.5k): 6.6 us per layer against 8.4 us
+// for the general split-K kernel.
+//
+// Roofline: HBM-bound, 2 * HD * 2 bytes per (key, kv head) + Q and O.
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.hpp"
+
+namespace svkv {
+
+namespace {
+
+constexpr int kBK = 64;                    // keys per K/V tile
+constexpr int kGroups = 2;                 // consumer warp groups, alternating tiles
+constexpr int kWarpsPerGroup = kBK / 16;   // 16 keys per warp
+constexpr int kCWarps = kGroups * kWarpsPerGroup;
+constexpr int kCThreads = kCWarps * 32;
+constexpr int kThreads = kCThreads + 32;   // + one TMA producer warp
+constexpr int kRows = 8;                   // query rows per kv head (N of the MMA)
+constexpr int kL2Ahead = 4;                // K/V tiles past the ring prefetched into L2 before the wait
+
+
+template <int HD>
+struct GqaCfg {
+    static constexpr int COLS = 64;                       // f16 columns per TMA box (128-byte swizzle span)
+    static constexpr int NB = HD / COLS;
+    static constexpr int PITCH = COLS * 2;
+    static constexpr int BOXB = kBK * PITCH;
+    static constexpr int TILE_B = NB * BOXB;              // K (or V) bytes per tile
+    static constexpr int STAGE_B = 2 * TILE_B;
+    static constexpr int STAGES = HD == 128 ? 3 : 6;      // ~96 KB ring: two CTAs per SM
+    static constexpr int RING_B = STAGES * STAGE_B;
+    static constexpr int CW_LD = HD + 4;                  // padded row of the warp-combine scratch
+    static constexpr int CW_B = kCWarps * kRows * CW_LD * 4;
+    static constexpr int CM_OFF = CW_B;                   // [warp][row] maxima, then sums
+    static_assert(CM_OFF + 2 * kCWarps * kRows * 4 <= RING_B, "combine scratch must fit in the stage ring");
+    static_assert(kRows * (HD / 4) <= kCThreads, "one (row, 4-column) group per consumer thread");
+    // cluster merge, leader CTA only, written by the other splits once every split has left the ring:
+    // partial O [split][row][HD] and (m, l) [split][row]
+    static constexpr int PUSH_O = 0;
+    static constexpr int PUSH_ML = 16 * kRows * HD * 4;
+    static_assert(PUSH_ML + 16 * kRows * 8 <= RING_B, "merge slots must fit in the stage ring");
+    static constexpr int BAR_OFF = RING_B;
+    static constexpr int SMEM = BAR_OFF + (2 * STAGES + 1) * 8 + 16;
+};
+
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory");
+}
+
+// transpose an 8x8 f16 fragment across the warp
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.L2 [%0];" ::"l"(p));
+}
+
+// asynchronous stores into another CTA's shared memory, counted on that CTA's mbarrier
+__device__ __forceinline__ void st_async_f4(uint32_t caddr, float4 v, uint32_t cbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(caddr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(cbar) : "memory");
+}
+__device__ __forceinline__ void st_async_f2(uint32_t caddr, float2 v, uint32_t cbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
+                 ::"r"(caddr), "f"(v.x), "f"(v.y), "r"(cbar) : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 2)
+fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                     const __grid_constant__ AttnArgs a) {
+    using C = GqaCfg<HD>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+    uint64_t* empty = full + C::STAGES;
+    uint64_t* mdata = empty + C::STAGES;                                        // leader: merge slots filled
+    volatile int* flag = reinterpret_cast<volatile int*>(mdata + 1);            // [0] abort
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // with a cluster merge, CTA 0 of each kv head's cluster is the merger (no K/V work) and CTA
+    // x >= 1 is split x - 1
+    const int kvh = blockIdx.y;
+    const bool merger = a.cluster_merge && blockIdx.x == 0;
+    const int split = a.cluster_merge ? (int)blockIdx.x - 1 : (int)blockIdx.x;
+    const int nq = a.T;                       // one query tile: every query of the launch
+    const int R = nq * a.G;                   // <= kRows, checked by the host
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarpsPerGroup);
+        }
+        mbar_init(mdata, 1);
+        flag[0] = 0;
+        fence_barrier_init();
+        // the other splits' partials: R rows of HD floats and an (m, l) pair each
+        if (merger) mbar_arrive_expect_tx(mdata, (uint32_t)(a.n_splits * R * (HD * 4 + 8)));
+    }
+    if (threadIdx.x == kCThreads) {
+        tma_prefetch_desc(&tmk);
+        tma_prefetch_desc(&tmv);
+    }
+    __syncthreads();
+    // every CTA of the cluster has initialised its barriers: the splits wait on this before their
+    // first remote store into the merger (the wait is long satisfied by then)
+    if (a.cluster_merge) cluster_arrive_relaxed();
+
+    if (merger) {
+        // ============================ merger: sum the splits' partials of this kv head
+        constexpr int G4m = HD / 4;
+        const int gi = threadIdx.x, n_gm = R * G4m;
+        pdl_wait();   // the output may still be in use by the previous launch
+        if (threadIdx.x == 0) pdl_trigger();   // the splits decide when the next launch may start
+        if (gi >= n_gm) return;
+        if (!mbar_wait(mdata, 0, a.err)) return;
+        const int r = gi / G4m, c = (gi % G4m) * 4;
+        const float* slot_o = reinterpret_cast<const float*>(smem + C::PUSH_O);
+        const float* slot_ml = reinterpret_cast<const float*>(smem + C::PUSH_ML);
+        const int ns = a.n_splits;
+        float2 ml[16];
+#pragma unroll
+        for (int sp = 0; sp < 16; sp++)
+            if (sp < ns) ml[sp] = *reinterpret_cast<const float2*>(&slot_ml[(sp * kRows + r) * 2]);
+        float MM = -INFINITY;
+#pragma unroll
+        for (int sp = 0; sp < 16; sp++)
+            if (sp < ns) MM = fmaxf(MM, ml[sp].x);
+        float LL = 0.0f;
+        float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int sp = 0; sp < 16; sp++) {
+            if (sp < ns && ml[sp].x != -INFINITY) {
+                const float w = fast_exp2(ml[sp].x - MM);
+                LL += ml[sp].y * w;
+                const float4 v = *reinterpret_cast<const float4*>(&slot_o[(sp * kRows + r) * HD + c]);
+                o4.x += v.x * w; o4.y += v.y * w; o4.z += v.z * w; o4.w += v.w * w;
+            }
+        }
+        const float inv = LL > 0.0f ? 1.0f / LL : 0.0f;
+        const int qi = r / a.G, g = r % a.G;
+        float* orow = a.out + (size_t)qi * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
+        *reinterpret_cast<float4*>(orow + c) = make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
+        return;
+    }
+
+    auto issue = [&](int j, int y) {
+        const int s = j % C::STAGES;
+        uint8_t* kst = smem + s * C::STAGE_B;
+        uint8_t* vst = kst + C::TILE_B;
+        mbar_arrive_expect_tx(&full[s], 2 * C::TILE_B);
+#pragma unroll
+        for (int b = 0; b < C::NB; b++) {
+            tma_load_2d(kst + b * C::BOXB, &tmk, kvh * HD + b * C::COLS, y, &full[s]);
+            tma_load_2d(vst + b * C::BOXB, &tmv, kvh * HD + b * C::COLS, y, &full[s]);
+        }
+    };
+
+    // ---- before the grid dependency: loads no earlier kernel of the step can change
+    const int ks0 = split * a.chunk;
+    const int kmax = min(a.S, ks0 + a.chunk);
+    int prefetched = 0;
+    if (warp == kCWarps) {
+        // L2 prefetch of the query rows (the previous kernel may still write them: only a hint)
+        const int q_es = a.q_type == SV_TYPE_F32 ? 4 : 2;
+        const int lines = HD * q_es / 128;
+        for (int i = lane; i < R * lines; i += 32) {
+            const int r = i / lines, qi = r / a.G, g = r % a.G;
+            prefetch_l2(a.q + (size_t)qi * a.q_nb_t + (size_t)(kvh * a.G + g) * a.q_nb_h + (i % lines) * 128);
+        }
+        if (lane == 0) {
+            // the split's last visible key, from a possibly stale n_past (a hint for the prefetch extent only)
+            int hint = a.causal_base;
+            if (a.causal_base_dev) hint = *reinterpret_cast<const volatile int*>(a.causal_base_dev);
+            const int pf_hi = a.mask_mode == SV_MASK_CAUSAL ? min(kmax, hint + nq + 1) : kmax;
+            const int nt_pf = pf_hi > ks0 ? (pf_hi - ks0 + kBK - 1) / kBK : 0;
+            int j0 = 0;
+            if (a.n_new > 0 && a.ring_prefill) {
+                // the kernel appends the step's rows itself and the launch before it wrote no cache rows
+                // while letting this one start early: the rows it reads are complete (the appended ones
+                // are patched in below), so the ring can fill now
+                const int nt_max = kmax > ks0 ? (kmax - ks0 + kBK - 1) / kBK : 0;
+                prefetched = min(nt_max, C::STAGES);
+                for (int j = 0; j < prefetched; j++) issue(j, a.row_base + ks0 + j * kBK);
+                j0 = prefetched;
+            }
+            // a few tiles past the ring only: long splits stream the rest (an L2 prefetch of a whole
+            // long context would evict itself before use)
+            const int pf_end = min(nt_pf, C::STAGES + kL2Ahead);
+            for (int j = j0; j < pf_end; j++) {
+#pragma unroll
+                for (int b = 0; b < C::NB; b++) {
+                    tma_prefetch_l2_2d(&tmk, kvh * HD + b * C::COLS, a.row_base + ks0 + j * kBK);
+                    tma_prefetch_l2_2d(&tmv, kvh * HD + b * C::COLS, a.row_base + ks0 + j * kBK);
+                }
+            }
+        }
+    }
+    if (warp < kCWarps) {
+        // bring the launch's parameters into this SM's constant cache now: after the wait every
+        // first touch of a cold parameter line would add a memory round trip to the critical path
+        asm volatile("" ::"l"(a.q), "l"(a.q_nb_t), "l"(a.q_nb_h), "r"(a.G), "r"(a.q_type), "f"(a.scale_log2),
+                     "l"(a.out), "l"(a.out_nb_t), "l"(a.out_nb_h), "r"(a.mask_mode), "r"(a.S), "r"(a.chunk));
+        asm volatile("" ::"r"(a.n_new), "l"(a.knew), "l"(a.vnew), "l"(a.new_nb_t), "l"(a.kc_w), "l"(a.vc_w),
+                     "l"(a.cache_row_bytes), "l"(a.err), "r"(a.cluster_merge), "r"(a.n_splits),
+                     "l"(a.causal_base_dev), "r"(a.causal_base), "r"(a.row_base));
+    }
+    pdl_wait();
+
+    // consumers: the query rows first (nothing below waits on them until the first tile)
+    const int gq = lane >> 2, tq = lane & 3;     // fragment row / column-pair index
+    const int q_es = a.q_type == SV_TYPE_F32 ? 4 : 2;
+    // Q^T as B fragments: rows k = head-dim, column n = query row gq
+    uint32_t qb[HD / 16][2];
+    if (warp < kCWarps) {
+        const bool valid = gq < R;
+        const uint8_t* qrow = nullptr;
+        if (valid) {
+            const int qi = gq / a.G, g = gq % a.G;
+            qrow = a.q + (size_t)qi * a.q_nb_t + (size_t)(kvh * a.G + g) * a.q_nb_h;
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int e = kk * 16 + h * 8 + 2 * tq;
+                uint32_t v = 0;
+                if (valid) {
+                    if (a.q_type == SV_TYPE_F32) {
+                        const float2 f = *reinterpret_cast<const float2*>(qrow + (size_t)e * q_es);
+                        v = pack_h2(f.x, f.y);
+                    } else {
+                        v = *reinterpret_cast<const uint32_t*>(qrow + (size_t)e * q_es);
+                    }
+                }
+                qb[kk][h] = v;
+            }
+        }
+    }
+
+    // ---- key range of this split
+    const int cbase = a.causal_base_dev ? __ldg(a.causal_base_dev) : a.causal_base;
+    const int khi = a.mask_mode == SV_MASK_CAUSAL ? min(a.S, cbase + nq) : a.S;
+    const int ks = ks0;
+    const int ke = min(khi, ks + a.chunk);
+    const int n_tiles = ke > ks ? (ke - ks + kBK - 1) / kBK : 0;
+    if (threadIdx.x == 0 && split == 0 && kvh == 0 && a.err && a.n_new > 0 && cbase + a.n_new > a.S)
+        atomicOr(a.err, ERRBIT_ROW_RANGE);   // appended rows past the grid's key bound are not written
+
+    if (warp == kCWarps) {
+        // ============================ TMA producer
+        if (lane == 0 && (n_tiles > 0 || prefetched > 0)) {
+            int issued = prefetched;
+            for (int j = prefetched; j < n_tiles; j++) {
+                const int s = j % C::STAGES;
+                if (j >= C::STAGES && !mbar_wait(&empty[s], ((j / C::STAGES) - 1) & 1, a.err)) {
+                    flag[0] = 1;
+                    break;
+                }
+                if (flag[0]) break;
+                issue(j, a.row_base + ks + j * kBK);
+                issued = j + 1;
+            }
+            // The next launch of the stream may start once every split has issued its last tile: its
+            // CTAs begin prefetching their own K/V at once, and triggering right after the grid
+            // dependency (measured: 7.7 vs 6.9 us per layer on config 2) floods HBM while this
+            // launch still waits on its query rows and last tiles.
+            pdl_trigger();
+            // never leave a bulk copy in flight into shared memory
+            for (int j = max(0, issued - C::STAGES); j < issued; j++)
+                mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1, a.err);
+        }
+        return;
+    }
+
+    // ============================ consumers
+    const int tid = threadIdx.x;                 // 0..255
+    const int grp = warp / kWarpsPerGroup, wig = warp % kWarpsPerGroup;
+
+    // per thread: query columns c0 = 2*tq, c1 = 2*tq + 1; visible-key limits
+    int qlim[2];
+    bool qvalid[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int r = 2 * tq + i;
+        qvalid[i] = r < R;
+        qlim[i] = a.mask_mode == SV_MASK_CAUSAL ? cbase + r / a.G : a.S - 1;
+    }
+
+    float o[HD / 16][4];
+#pragma unroll
+    for (int n = 0; n < HD / 16; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m[2] = {-INFINITY, -INFINITY};
+    float l[2] = {0.0f, 0.0f};
+
+    for (int j = grp; j < n_tiles; j += kGroups) {
+        const int s = j % C::STAGES;
+        // The two groups share the ring, so a group can reach stage s while the other group's tile
+        // j - STAGES still holds it (its fill may even be in flight).  A parity wait on full[s] alone
+        // cannot tell that phase from this one; waiting first for tile j - STAGES to be released
+        // (empty[s], which is at most one phase behind: this group released tile j - 2*STAGES)
+        // leaves exactly one pending fill of the stage, this tile's.
+        if (j >= C::STAGES && !mbar_wait(&empty[s], ((j / C::STAGES) - 1) & 1, a.err)) {
+            flag[0] = 1;
+            break;
+        }
+        if (!mbar_wait(&full[s], (j / C::STAGES) & 1, a.err)) {
+            flag[0] = 1;
+            break;
+        }
+        const int kw = ks + j * kBK + 16 * wig;   // first key of this warp
+        uint8_t* kst = smem + s * C::STAGE_B;
+        uint8_t* vst = kst + C::TILE_B;
+        if (kw < ke) {
+            // fused append: a key this launch appends is written to the cache from its source row and
+            // patched into the tile the TMA brought in (which may hold the old row)
+            if (a.n_new > 0 && kw < cbase + a.n_new && kw + 16 > cbase) {
+                constexpr int LANES = HD * 2 / 16;
+                const int k_lo = max(kw, cbase), k_hi = min(kw + 16, cbase + a.n_new);
+                for (int key = k_lo; key < k_hi; key++) {
+                    if (lane < LANES) {
+                        const size_t so = (size_t)(key - cbase) * a.new_nb_t + (size_t)kvh * HD * 2 + lane * 16;
+                        const uint4 kvec = *reinterpret_cast<const uint4*>(a.knew + so);
+                        const uint4 vvec = *reinterpret_cast<const uint4*>(a.vnew + so);
+                        const size_t co = (size_t)key * a.cache_row_bytes + (size_t)kvh * HD * 2 + lane * 16;
+                        *reinterpret_cast<uint4*>(a.kc_w + co) = kvec;
+                        *reinterpret_cast<uint4*>(a.vc_w + co) = vvec;
+                        const int row = key - (ks + j * kBK);
+                        const int e = lane * 8;
+                        const uint32_t off = (e / C::COLS) * C::BOXB + swz_off(row, e % C::COLS, C::PITCH);
+                        *reinterpret_cast<uint4*>(kst + off) = kvec;
+                        *reinterpret_cast<uint4*>(vst + off) = vvec;
+                    }
+                }
+                fence_proxy_async_smem();   // order these writes before the stage's next TMA fill
+                __syncwarp();
+            }
+            // ---- S^T = K Q^T: four accumulator chains over the head-dim blocks
+            float sacc[4][4] = {};
+            {
+                const int krow = 16 * wig + (lane & 15);
+                const uint32_t kbase = smem_u32(kst);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; kk++) {
+                    const int e = kk * 16 + 8 * (lane >> 4);
+                    uint32_t af[4];
+                    ldsm_x4(kbase + (e / C::COLS) * C::BOXB + swz_off(krow, e % C::COLS, C::PITCH), af[0], af[1],
+                            af[2], af[3]);
+                    mma_f16(sacc[kk & 3], af, qb[kk][0], qb[kk][1]);
+                }
+            }
+            // ---- scale + mask (log2 domain); element i: key kw + gq + 8*(i>>1), column 2*tq + (i&1)
+            float sv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int key = kw + gq + 8 * (i >> 1);
+                const int c = i & 1;
+                const bool vis = qvalid[c] && key < ke && key <= qlim[c];
+                sv[i] = vis ? ((sacc[0][i] + sacc[1][i]) + (sacc[2][i] + sacc[3][i])) * a.scale_log2 : -INFINITY;
+            }
+            // ---- online softmax per column over the warp's 16 keys (8 lanes share a column pair)
+            float alpha[2], mu[2];
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                float mx = fmaxf(sv[c], sv[c + 2]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(m[c], mx);
+                alpha[c] = m[c] == -INFINITY ? 0.0f : fast_exp2(m[c] - mn);
+                m[c] = mn;
+                mu[c] = mn == -INFINITY ? 0.0f : mn;
+            }
+            float p[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) p[i] = fast_exp2(sv[i] - mu[i & 1]);
+            // per-thread partial sums (the column's lanes are summed once at the end)
+            l[0] = l[0] * alpha[0] + (p[0] + p[2]);
+            l[1] = l[1] * alpha[1] + (p[1] + p[3]);
+#pragma unroll
+            for (int n = 0; n < HD / 16; n++) {
+                o[n][0] *= alpha[0];
+                o[n][1] *= alpha[1];
+                o[n][2] *= alpha[0];
+                o[n][3] *= alpha[1];
+            }
+            // ---- P^T as the B fragment: transpose the two 8x8 key blocks
+            const uint32_t pb0 = movmatrix_t(pack_h2(p[0], p[1]));   // keys 0-7
+            const uint32_t pb1 = movmatrix_t(pack_h2(p[2], p[3]));   // keys 8-15
+            // ---- O^T += V^T P^T
+            {
+                const int vrow = 16 * wig + (lane & 7) + 8 * (lane >> 4);
+                const uint32_t vbase = smem_u32(vst);
+#pragma unroll
+                for (int n = 0; n < HD / 16; n++) {
+                    const int e = n * 16 + 8 * ((lane >> 3) & 1);
+                    uint32_t af[4];
+                    ldsm_x4_t(vbase + (e / C::COLS) * C::BOXB + swz_off(vrow, e % C::COLS, C::PITCH), af[0], af[1],
+                              af[2], af[3]);
+                    mma_f16(o[n], af, pb0, pb1);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    // ============================ merge the eight warps
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+        l[c] += __shfl_xor_sync(0xffffffffu, l[c], 4);
+        l[c] += __shfl_xor_sync(0xffffffffu, l[c], 8);
+        l[c] += __shfl_xor_sync(0xffffffffu, l[c], 16);
+    }
+    consumer_sync();   // every warp is done with the stage ring: reuse it
+    float* cw = reinterpret_cast<float*>(smem);                   // [warp][row][CW_LD]
+    float* cm = reinterpret_cast<float*>(smem + C::CM_OFF);       // [warp][row]
+    float* cl = cm + kCWarps * kRows;                              // [warp][row]
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+        const int r = 2 * tq + c;
+        if (r < R) {
+            float* dst = cw + (warp * kRows + r) * C::CW_LD;
+#pragma unroll
+            for (int n = 0; n < HD / 16; n++) {
+                dst[n * 16 + gq] = o[n][c];
+                dst[n * 16 + gq + 8] = o[n][c + 2];
+            }
+            if (gq == 0) {
+                cm[warp * kRows + r] = m[c];
+                cl[warp * kRows + r] = l[c];
+            }
+        }
+    }
+    consumer_sync();
+
+    constexpr int G4 = HD / 4;
+    const int n_g = R * G4;
+    if (!a.cluster_merge) {   // one split: normalise and store
+        for (int gi = tid; gi < n_g; gi += kCThreads) {
+            const int r = gi / G4, c = (gi % G4) * 4;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kCWarps; w++) M = fmaxf(M, cm[w * kRows + r]);
+            float L = 0.0f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < kCWarps; w++) {
+                const float mw = cm[w * kRows + r];
+                const float sc = mw == -INFINITY ? 0.0f : fast_exp2(mw - M);
+                L += cl[w * kRows + r] * sc;
+                const float4 v = *reinterpret_cast<const float4*>(&cw[(w * kRows + r) * C::CW_LD + c]);
+                acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
+            }
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            const int qi = r / a.G, g = r % a.G;
+            float* orow = a.out + (size_t)qi * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
+            *reinterpret_cast<float4*>(orow + c) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
+        return;
+    }
+
+    // ---- split-K inside the cluster.  Each thread owns one (row, 4-column) group of this split's
+    // partial and pushes it, with its row's (m, l), into the merger's shared memory (st.async,
+    // counted on the merger's mbarrier); the split CTA then exits.  No split waits for another.
+    const int gi = tid;
+    if (gi >= n_g) return;
+    const int r = gi / G4, c = (gi % G4) * 4;
+    float M = -INFINITY, L = 0.0f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < kCWarps; w++) M = fmaxf(M, cm[w * kRows + r]);
+#pragma unroll
+    for (int w = 0; w < kCWarps; w++) {
+        const float mw = cm[w * kRows + r];
+        const float sc = mw == -INFINITY ? 0.0f : fast_exp2(mw - M);
+        L += cl[w * kRows + r] * sc;
+        const float4 v = *reinterpret_cast<const float4*>(&cw[(w * kRows + r) * C::CW_LD + c]);
+        acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
+    }
+    cluster_wait_acquire();   // the merger's barrier is initialised (arrived before the grid dependency)
+    const float* slot_o = reinterpret_cast<const float*>(smem + C::PUSH_O);
+    const float* slot_ml = reinterpret_cast<const float*>(smem + C::PUSH_ML);
+    const uint32_t bar = dsmem_map(smem_u32(mdata), 0);
+    st_async_f4(dsmem_map(smem_u32(&slot_o[(split * kRows + r) * HD + c]), 0), acc, bar);
+    if (c == 0) st_async_f2(dsmem_map(smem_u32(&slot_ml[(split * kRows + r) * 2]), 0), make_float2(M, L), bar);
+}
+
+template <int HD>
+cudaError_t prepare_gqa() {
+    static cudaError_t status = [] {
+        cudaError_t e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             GqaCfg<HD>::SMEM + 1024);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        return e;
+    }();
+    return status;
+}
+
+template <int HD>
+cudaError_t launch_gqa_t(const AttnArgs& a, const CUtensorMap* tk, const CUtensorMap* tv, cudaStream_t st) {
+    cudaError_t e = prepare_gqa<HD>();
+    if (e != cudaSuccess) return e;
+    // a cluster merge adds one merger CTA per kv head (cluster = splits + 1)
+    const int nx = a.cluster_merge ? a.n_splits + 1 : a.n_splits;
+    dim3 grid((unsigned)nx, (unsigned)a.NKV, 1u);
+    return launch_pdl_cluster(fa_decode_gqa_kernel<HD>, grid, dim3(kThreads), (size_t)GqaCfg<HD>::SMEM + 1024, st,
+                              a.cluster_merge ? nx : 1, *tk, *tv, a);
+}
+
+template <int HD>
+int max_cluster_gqa() {
+    static int v = -1;
+    if (v < 0) {
+        if (prepare_gqa<HD>() != cudaSuccess) {
+            cudaGetLastError();
+            v = 1;
+            return v;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(16, 1, 1);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = GqaCfg<HD>::SMEM + 1024;
+        int n = 0;
+        if (cudaOccupancyMaxPotentialClusterSize(&n, fa_decode_gqa_kernel<HD>, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 1;
+        }
+        v = n < 1 ? 1 : (n > 16 ? 16 : n);
+    }
+    return v;
+}
+
+}  // namespace
+
+bool decode_gqa_applies(int head_dim, int kv_type, int T, int G, int mask_mode) {
+    if (kv_type != SV_TYPE_F16 || (head_dim != 64 && head_dim != 128)) return false;
+    if (mask_mode != SV_MASK_CAUSAL && mask_mode != SV_MASK_NONE) return false;
+    return T * G <= kRows;
+}
+
+int decode_gqa_max_cluster(int head_dim) {
+    return head_dim == 128 ? max_cluster_gqa<128>() : head_dim == 64 ? max_cluster_gqa<64>() : 1;
+}
+
+cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
+                              cudaStream_t st) {
+    if (a.n_qtiles != 1 || a.T * a.G > kRows || (a.n_splits > 1 && !a.cluster_merge)) return cudaErrorInvalidValue;
+    switch (head_dim) {
+        case 64: return launch_gqa_t<64>(a, tk, tv, st);
+        case 128: return launch_gqa_t<128>(a, tk, tv, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace svkv

@@ -228,6 +228,7 @@ int sv_kv_destroy(sv_kv* kv) {
 int sv_kv_clear(sv_kv* kv, void* stream) {
     if (!kv) return SV_ERR_INVALID;
     DeviceGuard g(kv->device);
+    kv->rows_written_last = false;   // a memset is never overlapped by the next launch
     return cuda_status(cudaMemsetAsync(kv->buf, 0, kv->tensor_bytes * 2 * (size_t)kv->n_layer,
                                        static_cast<cudaStream_t>(stream)));
 }
@@ -285,21 +286,23 @@ int sv_kv_append(sv_kv* kv, int layer, const void* k, const void* v, int src_typ
     DeviceGuard g(kv->device);
     const int64_t ne0 = (int64_t)kv->n_kv_head * kv->head_dim;
     const size_t src_nb1 = row_bytes_of(src_type, ne0);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
     // K and V in one launch: blockIdx.y selects the tensor; V sits one tensor after K
     // in the cache buffer, and the V source is addressed relative to the K source.
     const uint8_t* kb = static_cast<const uint8_t*>(k);
     const uint8_t* vb = static_cast<const uint8_t*>(v);
+    cudaError_t e;
     if (vb > kb) {
-        return cuda_status(launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
-                                           src_nb1, n_rows, rows, base, kv->err, 2, kv->tensor_bytes,
-                                           (size_t)(vb - kb), static_cast<cudaStream_t>(stream)));
+        e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type, src_nb1,
+                            n_rows, rows, base, kv->err, 2, kv->tensor_bytes, (size_t)(vb - kb), st, nullptr, true);
+    } else {
+        e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type, src_nb1,
+                            n_rows, rows, base, kv->err, 1, 0, 0, st, nullptr, true);
+        if (e == cudaSuccess)
+            e = launch_set_rows(kv->tensor(layer, 1), kv->type, ne0, kv->n_ctx, kv->row_bytes, v, src_type, src_nb1,
+                                n_rows, rows, base, kv->err, 1, 0, 0, st, nullptr, true);
     }
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
-                                    src_nb1, n_rows, rows, base, kv->err, 1, 0, 0, st);
-    if (e == cudaSuccess)
-        e = launch_set_rows(kv->tensor(layer, 1), kv->type, ne0, kv->n_ctx, kv->row_bytes, v, src_type, src_nb1,
-                            n_rows, rows, base, kv->err, 1, 0, 0, st);
+    kv->rows_written_last = true;
     return cuda_status(e);
 }
 
@@ -314,15 +317,18 @@ int sv_kv_append_at(sv_kv* kv, int layer, const void* k, const void* v, int src_
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const uint8_t* kb = static_cast<const uint8_t*>(k);
     const uint8_t* vb = static_cast<const uint8_t*>(v);
-    if (vb > kb)
-        return cuda_status(launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
-                                           src_nb1, n_rows, nullptr, 0, kv->err, 2, kv->tensor_bytes,
-                                           (size_t)(vb - kb), st, base_dev));
-    cudaError_t e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type,
-                                    src_nb1, n_rows, nullptr, 0, kv->err, 1, 0, 0, st, base_dev);
-    if (e == cudaSuccess)
-        e = launch_set_rows(kv->tensor(layer, 1), kv->type, ne0, kv->n_ctx, kv->row_bytes, v, src_type, src_nb1,
-                            n_rows, nullptr, 0, kv->err, 1, 0, 0, st, base_dev);
+    cudaError_t e;
+    if (vb > kb) {
+        e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type, src_nb1,
+                            n_rows, nullptr, 0, kv->err, 2, kv->tensor_bytes, (size_t)(vb - kb), st, base_dev, true);
+    } else {
+        e = launch_set_rows(kv->tensor(layer, 0), kv->type, ne0, kv->n_ctx, kv->row_bytes, k, src_type, src_nb1,
+                            n_rows, nullptr, 0, kv->err, 1, 0, 0, st, base_dev, true);
+        if (e == cudaSuccess)
+            e = launch_set_rows(kv->tensor(layer, 1), kv->type, ne0, kv->n_ctx, kv->row_bytes, v, src_type, src_nb1,
+                                n_rows, nullptr, 0, kv->err, 1, 0, 0, st, base_dev, true);
+    }
+    kv->rows_written_last = true;
     return cuda_status(e);
 }
 
@@ -340,18 +346,35 @@ static bool clusters_enabled() {
     return on;
 }
 
+// SVKV_GQA=0 routes grouped-query decode to the general split-K kernel (A/B timing runs)
+static bool gqa_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("SVKV_GQA");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* tv, const CUtensorMap* tkp,
                          const CUtensorMap* tvp, int head_dim, int kv_type, AttnArgs& a, int span, bool window,
                          float* ws, size_t ws_bytes, int* tickets, int n_tickets, cudaStream_t st,
                          bool allow_cluster = false) {
-    (void)kvh;
+    // A fused append + attention may fill its K/V ring before its grid dependency resolves only if
+    // the launch before it on the stream did not write cache rows while letting it start early.
+    a.ring_prefill = (kvh && !kvh->rows_written_last) ? 1 : 0;
+    if (kvh) kvh->rows_written_last = false;
     // chunked prefill on the tensor-core kernel when it applies
     if (!window && tkp && tvp && a.mask_mode == SV_MASK_CAUSAL && a.T * a.G > 16) {
         return cuda_status(launch_prefill(a, head_dim, tkp, tvp, st));
     }
     const size_t ws_floats = ws ? ws_bytes / sizeof(float) : 0;
+    // grouped-query decode (one query tile of <= 8 rows per kv head) on the swap-AB kernel
+    const bool gqa = !window && gqa_enabled() && decode_gqa_applies(head_dim, kv_type, a.T, a.G, a.mask_mode);
     // split-K merged inside a thread-block cluster (DSMEM) when the splits fit in one cluster
-    const int cmax = (allow_cluster && !window && clusters_enabled()) ? decode_max_cluster(head_dim, kv_type) : 1;
+    // (the GQA kernel's cluster holds the splits plus one merger CTA)
+    const int cmax = (allow_cluster && !window && clusters_enabled())
+                         ? (gqa ? decode_gqa_max_cluster(head_dim) - 1 : decode_max_cluster(head_dim, kv_type))
+                         : 1;
     Plan p;
     bool use_cluster = false;
     if (cmax >= 2) {
@@ -373,6 +396,8 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     a.n_qtiles = p.n_qtiles;
     a.chunk = p.chunk;
     a.n_splits = p.n_splits;
+    if (gqa && a.n_qtiles == 1 && (a.n_splits == 1 || a.cluster_merge))
+        return cuda_status(launch_decode_gqa(a, head_dim, tk, tv, st));
     if (a.n_splits > 1 && !a.cluster_merge) {
         const size_t n_part = (size_t)a.NKV * a.n_qtiles * a.n_splits * 16;
         a.ws_o = ws;
@@ -646,6 +671,7 @@ int sv_kv_compact(sv_kv* kv, const sv_segment* segs, int n_segs, int dst_base, i
     }
     if (new_len) *new_len = (int)(dst_base + kept);
     DeviceGuard g(kv->device);
+    kv->rows_written_last = false;   // compaction launches are never overlapped by the next launch
     return cuda_status(launch_compact(kv, nullptr, segs, n_segs, dst_base, static_cast<cudaStream_t>(stream)));
 }
 

@@ -65,6 +65,9 @@ struct AttnArgs {
     uint8_t* kc_w;
     uint8_t* vc_w;
     size_t cache_row_bytes;
+    // the fused append may fill its K/V ring before the grid dependency resolves: the launch before
+    // it on the stream wrote no cache rows while letting it start early (host-tracked per handle)
+    int ring_prefill;
 };
 
 struct PrefillArgs;  // attn_prefill.cu
@@ -81,6 +84,9 @@ struct KvHandle {
     size_t ws_bytes = 0;
     int* tickets = nullptr;
     int n_tickets = 0;
+    // the last launch this handle enqueued was an append that lets the next launch start early;
+    // the next attention launch must then not read cache rows before its grid dependency resolves
+    bool rows_written_last = false;
     int* err = nullptr;                  // device error word
     uint8_t* scratch = nullptr;          // one tensor's worth of rows for compaction fallback
 
@@ -103,6 +109,11 @@ bool make_decode_tmap(CUtensorMap* m, const void* base, int kv_type, int head_di
                       size_t row_bytes, int64_t n_rows);
 size_t decode_partial_floats(int head_dim);   // floats per (tile, split) partial incl. m/l
 int decode_max_cluster(int head_dim, int kv_type);   // largest co-schedulable cluster (<= 16), 1 = none
+// GQA decode kernel (attn_decode_gqa.cu): f16 cache, HD 64/128, causal or no mask, T*G <= 8 rows
+bool decode_gqa_applies(int head_dim, int kv_type, int T, int G, int mask_mode);
+int decode_gqa_max_cluster(int head_dim);
+cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
+                              cudaStream_t st);
 int decode_block_keys();                       // BK
 cudaError_t launch_decode(const AttnArgs& a, int head_dim, int kv_type, const CUtensorMap* tk,
                           const CUtensorMap* tv, cudaStream_t st);
@@ -118,7 +129,7 @@ cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_ro
                             const void* src, int src_type, size_t src_nb1, int64_t n_rows,
                             const int32_t* rows, int64_t base, int* err, int n_tensors,
                             size_t dst_tensor_stride, size_t src_tensor_stride, cudaStream_t st,
-                            const int32_t* base_dev = nullptr);
+                            const int32_t* base_dev = nullptr, bool early_trigger = false);
 
 cudaError_t launch_counter_add(int32_t* counter, int n, int delta, cudaStream_t st);
 

@@ -365,3 +365,60 @@ def test_device_npast_graph_replay(orc, fused, NKV, HD, NH):
                 close(got[layer], ref)
     assert int(npast.item()) == n0 + steps
     assert kv.error_flags() == 0
+
+
+@pytest.mark.parametrize("fused,NH", [(True, 32), (True, 64), (False, 32)])
+def test_decode_long_context_back_to_back(orc, fused, NH):
+    """Many K/V tiles per split (16k keys), several layers, graph replays issued back to back with
+    no host sync in between (dependent launches overlap): the last step's outputs against the
+    oracle, every appended row bit-exact, no device error bit."""
+    L, NKV, HD, n0, steps = 4, 8, 128, 16000, 24
+    kv = sv.KvCache()
+    assert kv.alloc(0, L, NKV, HD, n0 + steps + 8)
+    g = torch.Generator(device=DEV)
+    g.manual_seed(31)
+    for layer in range(L):
+        kv.tensor(layer, 0).view(torch.float16)[:n0].normal_(generator=g)
+        kv.tensor(layer, 1).view(torch.float16)[:n0].normal_(generator=g)
+    ne0 = NKV * HD
+    q = orc.normal_f16(31, 1, L * NH * HD).reshape(L, 1, NH, HD)
+    k = orc.normal_f16(31, 2, L * ne0).reshape(L, 1, ne0)
+    v = orc.normal_f16(31, 3, L * ne0).reshape(L, 1, ne0)
+    td = lambda a: torch.from_numpy(a.view(np.float16)).to(DEV)
+    dq, dk, dv = td(q), td(k), td(v)
+    dout = torch.zeros(L, 1, NH, HD, dtype=torch.float32, device=DEV)
+    npast = torch.full((1,), n0, dtype=torch.int32, device=DEV)
+    st = torch.cuda.Stream()
+    max_keys = n0 + steps + 4
+
+    def step():
+        for layer in range(L):
+            if fused:
+                kv.attn_append_at(layer, dq[layer], dk[layer], dv[layer], npast, max_keys, 1 / np.sqrt(HD),
+                                  out=dout[layer], stream=st)
+            else:
+                kv.append_at(layer, dk[layer], dv[layer], npast, stream=st)
+                kv.attn_at(layer, dq[layer], npast, max_keys, 1 / np.sqrt(HD), out=dout[layer], stream=st)
+        sv.counter_add(npast, 1, stream=st)
+
+    with torch.cuda.stream(st):
+        step()
+        st.synchronize()
+        npast.fill_(n0)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            step()
+        for _ in range(steps):
+            graph.replay()
+        st.synchronize()
+    assert int(npast.item()) == n0 + steps
+    assert kv.error_flags() == 0
+    got = dout.cpu().numpy()
+    for layer in range(L):
+        kc = kv.tensor(layer, 0).cpu().numpy()
+        vc = kv.tensor(layer, 1).cpu().numpy()
+        for i in (0, steps // 2, steps - 1):
+            assert np.array_equal(kc[n0 + i].view(np.uint16), k[layer, 0])
+            assert np.array_equal(vc[n0 + i].view(np.uint16), v[layer, 0])
+        ref = ref_attn(orc, kv, layer, q[layer], n0 + steps - 1, 1 / np.sqrt(HD))
+        close(got[layer], ref)
