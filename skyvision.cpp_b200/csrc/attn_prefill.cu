@@ -6,42 +6,44 @@
 // over an f16 cache, causal mask as an in-kernel predicate
 // (set_causal_mask(mask, n_past, T), attention.hpp:60-67).
 //
-// Work unit: one 128-row query tile x one kv head x one split of its keys.  The
-// 128 rows pack 128/G queries x the G query heads of the kv head, so every K/V
-// tile feeds all heads of the GQA group.  The key range of a tile is cut into
-// n_splits contiguous parts; the splits of a tile run as one thread-block
-// cluster and merge their partial (m, l, O) through distributed shared memory,
-// so short prompts still cover every SM.  Warp roles (320 threads):
-//   warps 0-7  softmax: warps w and w+4 share TMEM lane quarter w%4 (32 rows)
-//              and split the columns (S columns [32h, 32h+32) of each 64-key
-//              tile, O columns [h*HD/2, (h+1)*HD/2)).  Load Q into shared memory
-//              (128-byte swizzled K-major); per tile read S with tcgen05.ld,
-//              apply scale and the causal predicate, exchange the half-row
-//              maxima (f16, mbarrier-synchronised), write P (f16) into one of
-//              two shared buffers and, only when a row's max grew by more than
-//              2^8, rescale that row of O in TMEM (tcgen05.ld/st).  Epilogue:
-//              O / l, or the cluster merge.
-//   warp 8     TMA producers: lane 0 streams K tiles, lane 1 V tiles, each into
-//              its own ring (5 stages at HD 128, 2 at HD 256); a K stage is
-//              refilled as soon as its S has completed, a V stage after its P.V.
-//   warp 9     MMA issuer (one thread), S double-buffered in TMEM so the
-//              tensor core computes S(j+1) while the softmax warps work on S(j):
-//                S  = Q K^T   M=128, N=64 keys, K=HD   (A, B K-major)
-//                O += P V     M=128, N=HD,      K=64   (A K-major, B MN-major)
-//              completions reach the other roles through tcgen05.commit on
-//              mbarriers.
-// TMEM: S buffers in columns [0, 64) and [64, 128), O in [128, 128 + HD).
+// Work unit: NQT query tiles of 128 rows (NQT = 2 at HD 128 when the chunk has two) x one kv
+// head x one split of its keys.  A tile's 128 rows pack 128/G queries x the G query heads of the
+// kv head, so every K/V tile feeds all heads of the GQA group, and with NQT = 2 each K/V tile
+// read from L2 feeds 256 rows.  Warp roles ((4*NQT + 2) warps):
+//   softmax warps (4 per query tile; warp w reads TMEM lane quarter w % 4, one row per thread):
+//              per 64-key tile read S (64 columns) with tcgen05.ld, apply scale and the causal
+//              predicate, take the row max, write P = exp2(S - m) as f16 over the first 32
+//              columns of the same TMEM buffer (the P.V MMA reads A from TMEM), and, only when
+//              the row max grew by more than 2^8, rescale the row of O in TMEM (exact: the final
+//              O / l uses the same stale max).  One exponential in four runs on the FMA pipe
+//              (exp2_fma) to take load off the SFU.
+//   TMA warp   lane 0 loads the query tiles (a 3D map over [T][NH][HD] whose {64, G, 128/G} box
+//              is one slab of a tile) and streams K tiles, lane 1 V tiles, each into its own ring
+//              (5 stages at HD 128, 2 at HD 256); a K stage is refilled as soon as its S has
+//              completed, a V stage after its P.V.
+//   MMA warp   (one thread) S double-buffered in TMEM per query tile, so the tensor core computes
+//              S(j+1) while the softmax warps work on S(j):
+//                S  = Q K^T   M=128, N=64 keys, K=HD   (A, B K-major, shared memory)
+//                O += P V     M=128, N=HD,      K=64   (A = P from TMEM, B = V MN-major)
+//              completions reach the other roles through tcgen05.commit on mbarriers (per
+//              parity of the tile index where a role can run a tile ahead).
+// TMEM per query tile: S/P buffers in columns [0, 64) and [64, 128), O in [128, 128 + HD).
+// Splits: when the units (query tiles x kv heads) are fewer than the SMs, the key range of a
+// unit is cut into up to 8 splits (one CTA per SM, no clusters, so every SM is usable).  The
+// splits take an arrival ticket; all but the last publish their partial (O, m, l) to the
+// handle's workspace, and the last waits (bounded) for them and merges with its own partial,
+// which never leaves TMEM.
 //
-// Measured limiter (round-trip probes and ncu): with 128 query rows per K/V
-// tile each SM must pull ~64 KB of K/V per 1.5 MFLOP-tile pair, and with the
-// ~3 us loaded L2 latency the ring that fits beside Q and P cannot keep that in
-// flight, so the tensor pipe idles (~15 % of peak).  Feeding 256 query rows per
-// K/V tile (two Q tiles per CTA, or a 2-SM cta_group::2 pair) is the next step.
+// Measured (config 2 splice tail, 384 over 4096 cached rows, one B200): 432 TFLOP/s over 36
+// layers.  In-kernel timestamps put the limiter in the softmax warps' per-tile chain (TMEM load,
+// row max, exponentials, P store: ~1500 cycles per 64-key tile) rather than in the tensor pipe
+// (~550 cycles of MMA per tile pair) or in L2.
 //
 // Roofline: tensor-bound.  Algorithmic FLOPs per launch = 4 * NH * HD * sum
 // over queries of visible keys (masked keys do not count).
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 
 #include "common.cuh"
 #include "internal.hpp"
@@ -50,8 +52,6 @@ namespace svkv {
 
 namespace {
 
-constexpr int kPThreads = 320;          // 8 softmax warps, 1 TMA warp, 1 MMA warp
-constexpr int kSoftmaxThreads = 256;
 constexpr float kRescaleLog2 = 8.0f;     // rescale O only when the max grows by > 2^8
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
@@ -111,35 +111,49 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
         : "memory");
 }
 
+// 2^x on the FMA pipe, for part of the softmax exponentials (the SFU's ex2 rate, 16 per clock per
+// SM, is below the tensor pipe's rate for 64-key tiles).  x = n + f with n = round(x), f in
+// [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here for minimax relative error on that interval
+// (iteratively reweighted least squares; max relative error 7.5e-5 in f32, under the f16 rounding
+// P gets anyway), and 2^n added into the exponent field.  x is clamped at -126 (2^-126 rounds to 0
+// in f16), and x <= 128 holds because P is taken against a running max that trails the true max
+// by at most 2^8.
+__device__ __forceinline__ float exp2_fma(float x) {
+    x = fmaxf(x, -126.0f);
+    const float t = x + 12582912.0f;             // 1.5 * 2^23: round(x) lands in the low mantissa bits
+    const float f = x - (t - 12582912.0f);
+    const float p = fmaf(fmaf(fmaf(0.05517166853f, f, 0.24261114001f), f, 0.69326096773f), f, 0.99992805719f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-template <int HD>
+// NQT query tiles of 128 rows per CTA share every K/V tile (NQT = 2 at HD 128).
+template <int HD, int NQT>
 struct PreCfg {
-    static constexpr int BN = 64;                         // keys per tile (one 128-byte swizzle row of P)
-    static constexpr int NS = HD >= 256 ? 2 : 5;          // K/V stages (shared memory budget)
+    static constexpr int BN = 64;                         // keys per tile
     static constexpr int BOX_ROW = 128;                   // bytes per swizzled row (64 f16)
-    static constexpr int QBOX = 128 * BOX_ROW;            // one 64-column slab of the Q tile
-    static constexpr int Q_B = (HD / 64) * QBOX;
+    static constexpr int QBOX = 128 * BOX_ROW;            // one 64-column slab of a Q tile
+    static constexpr int Q_B = (HD / 64) * QBOX;          // one Q tile
     static constexpr int KBOX = BN * BOX_ROW;             // one 64-column slab of a K or V tile
     static constexpr int KV_B = (HD / 64) * KBOX;         // K (or V) bytes per stage
     static constexpr int STAGE_B = 2 * KV_B;
-    static constexpr int P_B = 128 * BOX_ROW;             // 128 rows x 64 keys of P (one of two buffers)
+    static constexpr int NS_FIT = (227 * 1024 - NQT * Q_B - 2048) / STAGE_B;
+    static constexpr int NS = NS_FIT > 5 ? 5 : NS_FIT;    // K/V stages
+    static_assert(NS >= 2, "K/V ring needs two stages");
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_ST = OFF_Q + Q_B;
-    static constexpr int OFF_P = OFF_ST + NS * STAGE_B;
-    static constexpr int OFF_X = OFF_P + 2 * P_B;        // row-max exchange: f16 [2 parities][2 halves][128]
-    static constexpr int OFF_BAR = OFF_X + 2 * 2 * 128 * 2;
-    static constexpr int N_BAR = 4 * NS + 7 + 4;         // K and V rings, + one exchange barrier per lane quarter
+    static constexpr int OFF_ST = OFF_Q + NQT * Q_B;
+    static constexpr int OFF_BAR = OFF_ST + NS * STAGE_B;
+    static constexpr int N_BAR = 4 * NS + 1 + NQT * 6;
     static constexpr int SMEM = OFF_BAR + N_BAR * 8 + 16;
-    static constexpr int OCOL = 128;                      // S buffers at columns 0 and 64
-    static constexpr int TMEM_COLS = (OCOL + HD) <= 256 ? 256 : 512;
-    // cluster merge staging after the main loop: partial O [128][HD] f32 over Q + the ring,
-    // and (m, l) per row in the P region
-    static constexpr int OFF_PO = 0;
-    static constexpr int OFF_PM = OFF_P;
-    static_assert(128 * HD * 4 <= OFF_P, "partial O must fit in front of the P buffer");
-    static_assert(128 * 2 * 4 <= P_B, "row statistics must fit in the P buffer");
+    static_assert(SMEM + 1024 <= 227 * 1024, "shared memory budget");
+    static constexpr int QCOLS = 128 + HD;                // per Q tile: S/P buffers [0, 64) and [64, 128), O after
+    static constexpr int TMEM_COLS = NQT * QCOLS <= 256 ? 256 : 512;
+    static_assert(NQT * QCOLS <= 512, "TMEM budget");
+    static constexpr int SM_WARPS = 4 * NQT;              // softmax warps: one row per thread
+    static constexpr int THREADS = (SM_WARPS + 2) * 32;   // + TMA producer warp + MMA warp
+    static constexpr int ROWS = NQT * 128;
 };
 
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag) {
@@ -162,11 +176,33 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return __all_sync(0xffffffffu, ok);
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kPThreads, 1)
+// O += P V with P (f16, K-major) read from TMEM
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "setp.ne.b32 p, %4, 0;\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
+        "}\n" ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// Named barrier of the softmax warps.  Code before it may have run on one lane only (a ticket,
+// a bounded spin), so the warp reconverges first: the barrier instruction must be executed by
+// whole warps.
+template <int kSoftmaxWarps>
+__device__ __forceinline__ void softmax_sync() {
+    __syncwarp();
+    asm volatile("barrier.sync 2, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+}
+
+template <int HD, int NQT>
+__global__ void __launch_bounds__(PreCfg<HD, NQT>::THREADS, 1)
 fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                  const __grid_constant__ AttnArgs a) {
-    using C = PreCfg<HD>;
+                  const __grid_constant__ CUtensorMap tmq, const __grid_constant__ AttnArgs a) {
+    using C = PreCfg<HD, NQT>;
+    constexpr int kSoftmaxWarps = C::SM_WARPS;
+    constexpr int kTmaWarp = kSoftmaxWarps;   // then one MMA-issuer warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -176,18 +212,22 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     uint64_t* full_v = bars + 2 * C::NS;  // [NS]
     uint64_t* empty_v = bars + 3 * C::NS; // [NS]
     uint64_t* q_full = bars + 4 * C::NS;
-    uint64_t* s_full = q_full + 1;        // [2] per S buffer
-    uint64_t* p_full = q_full + 3;
-    uint64_t* o_done = q_full + 4;        // [2] per P buffer: P.V of the tiles that used it
-    uint64_t* xbar = q_full + 6;          // [4] the two softmax warps of a lane quarter exchanged their halves
+    uint64_t* s_full = q_full + 1;        // [NQT][2] per Q tile and S buffer
+    // [NQT][2] P(i) written, by the parity of i: the softmax warps can finish tile i+1 before the
+    // MMA warp has taken P(i) (S(i+1) is issued first), so one barrier would be two phases ahead
+    uint64_t* p_full = s_full + 2 * NQT;
+    uint64_t* o_done = p_full + 2 * NQT;  // [NQT][2] P.V(i) of the Q tile, by the parity of i
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + C::N_BAR);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* last_flag = abort_flag + 1;   // split merge: this CTA is the last split of its unit
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x, qt = blockIdx.y, kvh = blockIdx.z;
+    const int split = blockIdx.x, qp = blockIdx.y, kvh = blockIdx.z;
     const int ns = a.n_splits;
     const int QPT = 128 / a.G;
-    const int t0 = qt * QPT;
+    const int t0 = qp * NQT * QPT;                       // first query of the CTA's first Q tile
+    const int nq_all = min(NQT * QPT, a.T - t0);         // queries of this CTA
+    const int nqt = (nq_all + QPT - 1) / QPT;            // Q tiles with any query (1..NQT)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::NS; s++) {
@@ -196,14 +236,17 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
             mbar_init(&full_v[s], 1);
             mbar_init(&empty_v[s], 1);
         }
-        // the softmax warps arrive once per warp (lane 0 after __syncwarp)
-        mbar_init(q_full, kSoftmaxThreads / 32);
-        mbar_init(&s_full[0], 1);
-        mbar_init(&s_full[1], 1);
-        mbar_init(p_full, kSoftmaxThreads / 32);
-        mbar_init(&o_done[0], 1);
-        mbar_init(&o_done[1], 1);
-        for (int k = 0; k < 4; k++) mbar_init(&xbar[k], 2);
+        // f16 queries arrive by TMA (one arrival with the byte count); f32 ones are converted by the
+        // softmax warps (one arrival per warp)
+        mbar_init(q_full, a.q_tma ? 1 : kSoftmaxWarps);
+        for (int q = 0; q < NQT; q++) {
+            mbar_init(&s_full[2 * q], 1);
+            mbar_init(&s_full[2 * q + 1], 1);
+            mbar_init(&p_full[2 * q], 4);
+            mbar_init(&p_full[2 * q + 1], 4);
+            mbar_init(&o_done[2 * q], 1);
+            mbar_init(&o_done[2 * q + 1], 1);
+        }
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -212,9 +255,10 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                      "r"((uint32_t)C::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == kTmaWarp && lane == 0) {
         tma_prefetch_desc(&tmk);
         tma_prefetch_desc(&tmv);
+        if (a.q_tma) tma_prefetch_desc(&tmq);
     }
     tc_fence_before();
     __syncthreads();
@@ -223,40 +267,44 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     pdl_wait();                      // everything above overlapped the previous kernel
     if (threadIdx.x == 0) pdl_trigger();
     const int cbase = a.causal_base_dev ? __ldg(a.causal_base_dev) : a.causal_base;
-    const int nq = min(QPT, a.T - t0);
-    const int kend = min(a.S, cbase + t0 + nq);                 // keys [0, kend) reach some row
+    const int kend = min(a.S, cbase + t0 + nq_all);             // keys [0, kend) reach some row
     const int nt = (kend + C::BN - 1) / C::BN;                  // tiles of the whole key range
     const int j0 = (int)((long long)nt * split / ns);           // this split's tiles [j0, j1)
     const int j1 = (int)((long long)nt * (split + 1) / ns);
     const int n = j1 - j0;
-    // The query tiles of one kv head stream the same K/V tiles; each starts at a different
-    // rotation of its range so they do not hit the same L2 lines in lockstep (the online
-    // softmax does not depend on the order of the tiles).
-    const int rot = n > 0 ? (qt * 7) % n : 0;
+    // The CTAs of one kv head stream the same K/V tiles; each starts at a different rotation of
+    // its range so they do not hit the same L2 lines in lockstep (the online softmax does not
+    // depend on the order of the tiles).
+    const int rot = n > 0 ? (qp * 7) % n : 0;
     auto tile_of = [&](int i) { return j0 + (i + rot) % n; };
 
-    if (warp < 8) {
-        // ============================ softmax warps
-        // Warps w and w+4 read the same TMEM lane quarter (w % 4), i.e. the same 32 rows, and
-        // split the columns: half ch = w / 4 owns S columns [32ch, 32ch + 32) of every tile and
-        // O columns [ch*HD/2, (ch+1)*HD/2).  The two halves exchange row maxima through shared
-        // memory once per tile and their partial sums once at the end.
-        const int quarter = warp & 3, ch = warp >> 2;
+    if (warp < kSoftmaxWarps) {
+        // ============================ softmax warps: one row of one Q tile per thread
+        // Q tile qtl = warp / 4, TMEM lane quarter warp % 4 (rows 32*quarter + lane).  Per key tile:
+        // S (64 columns) from TMEM, scale and causal mask, row max, P = exp2(S - m) written back as
+        // f16 over the first 32 columns of the same TMEM buffer (the P.V MMA reads it from there),
+        // and, only when the row max grew by more than 2^8, O rescaled in TMEM.
+        const int qtl = warp >> 2, quarter = warp & 3;
+        const bool tile_live = qtl < nqt;
         const int r = quarter * 32 + lane;               // row = TMEM lane
-        const int qi = r / a.G, g = r % a.G;
+        const int qi = qtl * QPT + r / a.G, g = r % a.G;
         const int t = t0 + qi;
-        const bool valid = qi < nq;
+        const bool valid = qi < nq_all;
         const int qpos = cbase + min(t, a.T - 1);        // invalid rows mirror the last query
-        const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+        const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(qtl * C::QCOLS);
         const float c = a.scale_log2;
-        __half* xch = reinterpret_cast<__half*>(smem + C::OFF_X);   // [2 parities][2 halves][128 rows]
-        uint64_t* xb = &xbar[quarter];
-        // ---- Q: each thread loads half of its row (128-byte swizzled, K-major)
-        {
+        uint64_t* sf = &s_full[2 * qtl];
+        uint64_t* pf = &p_full[2 * qtl];
+        // o_done[2q + b] completes with P.V(i) for i % 2 == b.  When S(i) is visible, P.V(i-2) has
+        // completed (it was issued before S(i)), so a wait below is never two phases behind.
+        uint64_t* od = &o_done[2 * qtl];
+        // ---- Q: f16 queries come by TMA from the producer warp; otherwise (f32, or strides a tensor
+        // map cannot describe) each thread loads and converts its row (128-byte swizzled, K-major)
+        if (!a.q_tma) {
             const uint8_t* qrow = a.q + (size_t)(valid ? t : 0) * a.q_nb_t + (size_t)(kvh * a.G + g) * a.q_nb_h;
-            uint8_t* qs = smem + C::OFF_Q;
+            uint8_t* qs = smem + C::OFF_Q + qtl * C::Q_B;
 #pragma unroll 4
-            for (int e = ch * (HD / 2); e < (ch + 1) * (HD / 2); e += 8) {
+            for (int e = 0; e < HD; e += 8) {
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if (valid) {
                     if (a.q_type == SV_TYPE_F32) {
@@ -276,37 +324,31 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
             __syncwarp();
             if (lane == 0) mbar_arrive(q_full);
         }
-        float m_use = -INFINITY, l = 0.0f;               // l: this half's partial row sum
+        float m_use = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (int i = 0; i < n; i++) {
-            if (!warp_wait(&s_full[i & 1], (i >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
+        const int n_mine = tile_live ? n : 0;
+        for (int i = 0; i < n_mine; i++) {
+            if (!warp_wait(&sf[i & 1], (i >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const int kb = tile_of(i) * C::BN + ch * 32;  // first key of this half
-            float s[32];
-            tmem_ld32(lane_addr + (i & 1) * C::BN + ch * 32, s);
+            const int kb = tile_of(i) * C::BN;           // first key of the tile
+            const uint32_t sbuf = lane_addr + (i & 1) * C::BN;
+            float s[64];
+            tmem_ld32(sbuf, s);
+            tmem_ld32(sbuf + 32, s + 32);
             tmem_wait_ld();
             // keys past the row's position (or past kend) are masked; only the last tiles have any
-            if (kb + 31 > qpos || kb + 32 > kend) {
+            if (kb + 63 > qpos || kb + 64 > kend) {
 #pragma unroll
-                for (int k = 0; k < 32; k++)
+                for (int k = 0; k < 64; k++)
                     if (kb + k > qpos || kb + k >= kend) s[k] = -INFINITY;
             }
             float m8[8];
 #pragma unroll
-            for (int k = 0; k < 8; k++) m8[k] = fmaxf(fmaxf(s[k], s[k + 8]), fmaxf(s[k + 16], s[k + 24]));
-            float mr = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-            {
-                // both halves use the f16-rounded maxima, so they agree on the row's offset; the
-                // offset only has to be near the true maximum (p stays far below f16 overflow)
-                __half* slot = xch + (i & 1) * 2 * 128;
-                const __half mine = __float2half_ru(fminf(mr, 65504.0f));
-                slot[ch * 128 + r] = mine;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(xb);
-                if (!warp_wait(xb, i & 1, a.err, abort_flag)) { ok = false; break; }
-                mr = fmaxf(__half2float(mine), __half2float(slot[(1 - ch) * 128 + r]));
-            }
+            for (int k = 0; k < 8; k++)
+                m8[k] = fmaxf(fmaxf(fmaxf(s[k], s[k + 8]), fmaxf(s[k + 16], s[k + 24])),
+                              fmaxf(fmaxf(s[k + 32], s[k + 40]), fmaxf(s[k + 48], s[k + 56])));
+            const float mr = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             const float mt = mr * c;                     // scale > 0 commutes with max
             float alpha = 1.0f;
             bool resc = false;
@@ -317,109 +359,196 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                 m_use = mt;
                 resc = true;
             }
-            // P buffer i&1 was last read by P.V(i-2); a rescale of O needs P.V(i-1) complete
-            if (i >= 2) {
-                if (!warp_wait(&o_done[i & 1], ((i - 2) >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
-                tc_fence_after();
-            }
-            const bool any_resc = __any_sync(0xffffffffu, resc);
-            if (any_resc) {
-                if (!warp_wait(&o_done[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
+            if (__any_sync(0xffffffffu, resc)) {
+                // O is stable once P.V(i-1) has completed
+                if (!warp_wait(&od[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll 1
-                for (int cc = ch * (HD / 2); cc < (ch + 1) * (HD / 2); cc += 32) {
+                for (int cc = 0; cc < HD; cc += 32) {
                     float o[32];
-                    tmem_ld32(lane_addr + C::OCOL + cc, o);
+                    tmem_ld32(lane_addr + 128 + cc, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int k = 0; k < 32; k++) o[k] *= alpha;
-                    tmem_st32(lane_addr + C::OCOL + cc, o);
+                    tmem_st32(lane_addr + 128 + cc, o);
                 }
-                tmem_wait_st();
             }
             const float mneg = m_use == -INFINITY ? 0.0f : -m_use;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-            uint8_t* ps = smem + C::OFF_P + (i & 1) * C::P_B;
+            uint32_t pk[32];
 #pragma unroll
-            for (int cc = 0; cc < 32; cc += 8) {
-                float p[8];
-#pragma unroll
-                for (int k = 0; k < 8; k++) {
-                    p[k] = fast_exp2(fmaf(s[cc + k], c, mneg));
-                    sum4[k & 3] += p[k];
-                }
-                uint4 v;
-                v.x = pack_h2(p[0], p[1]);
-                v.y = pack_h2(p[2], p[3]);
-                v.z = pack_h2(p[4], p[5]);
-                v.w = pack_h2(p[6], p[7]);
-                *reinterpret_cast<uint4*>(ps + swz_off(r, ch * 32 + cc, 128)) = v;
+            for (int k = 0; k < 64; k += 4) {
+                // three of every four on the SFU, one on the FMA pipe
+                const float p0 = fast_exp2(fmaf(s[k], c, mneg));
+                const float p1 = fast_exp2(fmaf(s[k + 1], c, mneg));
+                const float p2 = fast_exp2(fmaf(s[k + 2], c, mneg));
+                const float p3 = exp2_fma(fmaf(s[k + 3], c, mneg));
+                sum4[(k >> 2) & 3] += (p0 + p1) + (p2 + p3);
+                pk[k >> 1] = pack_h2(p0, p1);
+                pk[(k >> 1) + 1] = pack_h2(p2, p3);
             }
+            // P over the first 32 columns of this tile's S buffer (S(i+2) reuses the buffer only
+            // after P.V(i) has been issued, and the tensor pipe runs in order)
+            tmem_st32(sbuf, reinterpret_cast<const float*>(pk));
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-            fence_proxy_async_smem();
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&pf[i & 1]);
         }
-        if (n > 0 && ok && !warp_wait(&o_done[(n - 1) & 1], ((n - 1) >> 1) & 1, a.err, abort_flag)) ok = false;
+        if (n_mine > 0 && ok && !warp_wait(&od[(n_mine - 1) & 1], ((n_mine - 1) >> 1) & 1, a.err, abort_flag))
+            ok = false;
         tc_fence_after();
-        // the row sum: both halves' partial sums (a slot set the last tile did not use)
-        float L = l;
-        if (ok) {
-            // P buffer 1 is free once the last P.V has completed: it carries the f32 half sums
-            float* lx = reinterpret_cast<float*>(smem + C::OFF_P + C::P_B);
-            lx[ch * 128 + r] = l;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(xb);
-            if (warp_wait(xb, n & 1, a.err, abort_flag)) L = l + lx[(1 - ch) * 128 + r];
-        }
+        const float L = l;
         float* orow = valid ? a.out + (size_t)t * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h : nullptr;
         if (ns == 1) {
-            // ---- single split: this half of O / L straight out of TMEM
+            // ---- single split: O / L straight out of TMEM
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            if (tile_live) {
 #pragma unroll 1
-            for (int cc = ch * (HD / 2); cc < (ch + 1) * (HD / 2); cc += 32) {
-                float o[32];
-                if (n > 0) {
-                    tmem_ld32(lane_addr + C::OCOL + cc, o);
-                    tmem_wait_ld();
-                } else {
+                for (int cc = 0; cc < HD; cc += 32) {
+                    float o[32];
+                    if (n > 0) {
+                        tmem_ld32(lane_addr + 128 + cc, o);
+                        tmem_wait_ld();
+                    } else {
 #pragma unroll
-                    for (int k = 0; k < 32; k++) o[k] = 0.0f;
-                }
-                if (valid) {
+                        for (int k = 0; k < 32; k++) o[k] = 0.0f;
+                    }
+                    if (valid) {
 #pragma unroll
-                    for (int k = 0; k < 32; k += 4)
-                        *reinterpret_cast<float4*>(orow + cc + k) =
-                            make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
+                        for (int k = 0; k < 32; k += 4)
+                            *reinterpret_cast<float4*>(orow + cc + k) =
+                                make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
+                    }
                 }
             }
         } else {
-            // ---- split: stage the unnormalised partial in shared memory for the cluster merge
-            // (the last tile's P.V is complete, so Q, the K/V ring and P are free)
-            float* po = reinterpret_cast<float*>(smem + C::OFF_PO);
-            float* pm = reinterpret_cast<float*>(smem + C::OFF_PM);
+            // ---- split: the splits of a unit (query tiles x kv head) take an arrival ticket; all
+            // but the last publish their partial (unnormalised O, m, l) to the workspace and count
+            // it, and the last waits for those counts and merges them with its own partial, which
+            // stays in TMEM.  Workspace layout [split][col/4][row] float4: a warp's 32 rows are one
+            // coalesced 512-byte access per column group.  Counters: tickets[2u] arrivals,
+            // tickets[2u + 1] published partials; the merging CTA resets both.
+            const int unit = qp * a.NKV + kvh;
+            const int row = qtl * 128 + r;
+            const bool have = n > 0 && tile_live && ok;
+            int* arrive_ctr = &a.tickets[2 * unit];
+            int* pub_ctr = &a.tickets[2 * unit + 1];
+            softmax_sync<kSoftmaxWarps>();
+            if (threadIdx.x == 0) *last_flag = atomicAdd(arrive_ctr, 1) == ns - 1;
+            softmax_sync<kSoftmaxWarps>();
+            if (!*last_flag) {
+                float4* wo = reinterpret_cast<float4*>(a.ws_o) + (size_t)(unit * ns + split) * (HD / 4) * C::ROWS;
+                float2* wml = reinterpret_cast<float2*>(a.ws_ml) + (size_t)(unit * ns + split) * C::ROWS;
 #pragma unroll 1
-            for (int cc = ch * (HD / 2); cc < (ch + 1) * (HD / 2); cc += 32) {
-                float o[32];
-                if (n > 0) {
-                    tmem_ld32(lane_addr + C::OCOL + cc, o);
-                    tmem_wait_ld();
-                } else {
+                for (int cc = 0; cc < HD; cc += 32) {
+                    float o[32];
+                    if (have) {
+                        tmem_ld32(lane_addr + 128 + cc, o);
+                        tmem_wait_ld();
+                    } else {
 #pragma unroll
-                    for (int k = 0; k < 32; k++) o[k] = 0.0f;
+                        for (int k = 0; k < 32; k++) o[k] = 0.0f;
+                    }
+#pragma unroll
+                    for (int k = 0; k < 32; k += 4)
+                        wo[(size_t)((cc + k) / 4) * C::ROWS + row] = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
                 }
+                wml[row] = make_float2(have ? m_use : -INFINITY, have ? L : 0.0f);
+                __threadfence();
+                softmax_sync<kSoftmaxWarps>();
+                if (threadIdx.x == 0) atomicAdd(pub_ctr, 1);
+            } else {
+                // wait (bounded) until the other splits, all running, have published
+                if (threadIdx.x == 0) {
+                    const uint64_t tw = globaltimer_ns();
+                    bool done = false;
+                    while (!done) {
+                        done = *reinterpret_cast<volatile int*>(pub_ctr) >= ns - 1;
+                        if (!done && globaltimer_ns() - tw > kWaitLimitNs) {
+                            if (a.err) atomicOr(a.err, ERRBIT_TIMEOUT);
+                            break;
+                        }
+                    }
+                    *last_flag = done ? 1 : 2;
+                    *arrive_ctr = 0;                         // ready for the next launch
+                    *pub_ctr = 0;
+                }
+                softmax_sync<kSoftmaxWarps>();
+                __threadfence();
+                // warp-uniform condition: the TMEM loads below are whole-warp instructions; only the
+                // output store depends on the row being a real query
+                if (*last_flag == 1 && tile_live) {
+                    const float2* uml = reinterpret_cast<const float2*>(a.ws_ml) + (size_t)unit * ns * C::ROWS;
+                    const float4* uo = reinterpret_cast<const float4*>(a.ws_o) + (size_t)unit * ns * (HD / 4) * C::ROWS;
+                    float wsp[8];
+                    float2 mls[8];
+                    float M = have ? m_use : -INFINITY;
 #pragma unroll
-                for (int k = 0; k < 32; k += 4)
-                    *reinterpret_cast<float4*>(&po[r * HD + cc + k]) = make_float4(o[k], o[k + 1], o[k + 2], o[k + 3]);
-            }
-            if (ch == 0) {
-                pm[r * 2] = n > 0 ? m_use : -INFINITY;
-                pm[r * 2 + 1] = n > 0 ? L : 0.0f;
+                    for (int sp = 0; sp < 8; sp++) {
+                        if (sp < ns && sp != split) {
+                            mls[sp] = __ldcg(&uml[(size_t)sp * C::ROWS + row]);
+                            M = fmaxf(M, mls[sp].x);
+                        }
+                    }
+                    const float w_own = (have && m_use != -INFINITY) ? fast_exp2(m_use - M) : 0.0f;
+                    float LL = have ? L * w_own : 0.0f;
+#pragma unroll
+                    for (int sp = 0; sp < 8; sp++) {
+                        if (sp < ns && sp != split) {
+                            wsp[sp] = mls[sp].x == -INFINITY ? 0.0f : fast_exp2(mls[sp].x - M);
+                            LL += mls[sp].y * wsp[sp];
+                        }
+                    }
+                    const float inv = LL > 0.0f ? 1.0f / LL : 0.0f;
+#pragma unroll 1
+                    for (int cc = 0; cc < HD; cc += 32) {
+                        float o[32];
+                        if (have) {
+                            tmem_ld32(lane_addr + 128 + cc, o);
+                            tmem_wait_ld();
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 32; k++) o[k] = 0.0f;
+                        }
+#pragma unroll
+                        for (int k = 0; k < 32; k++) o[k] *= w_own;
+#pragma unroll
+                        for (int sp = 0; sp < 8; sp++) {
+                            if (sp < ns && sp != split) {
+                                float4 v[8];
+#pragma unroll
+                                for (int u = 0; u < 8; u++)
+                                    v[u] = __ldcg(&uo[((size_t)sp * (HD / 4) + cc / 4 + u) * C::ROWS + row]);
+                                const float w = wsp[sp];
+#pragma unroll
+                                for (int u = 0; u < 8; u++) {
+                                    o[4 * u] += v[u].x * w; o[4 * u + 1] += v[u].y * w;
+                                    o[4 * u + 2] += v[u].z * w; o[4 * u + 3] += v[u].w * w;
+                                }
+                            }
+                        }
+                        if (valid) {
+#pragma unroll
+                            for (int k = 0; k < 32; k += 4)
+                                *reinterpret_cast<float4*>(orow + cc + k) =
+                                    make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
+                        }
+                    }
+                }
             }
         }
-    } else if (warp == 8) {
-        // ============================ TMA producers: lane 0 streams K tiles, lane 1 V tiles
+    } else if (warp == kTmaWarp) {
+        // ============================ TMA producers: lane 0 loads the Q tiles, then streams K tiles; lane 1 V
+        if (lane == 0 && a.q_tma) {
+            // box {64 columns, G heads, QPT queries} = the 128 rows of a Q tile in row order qi*G + g
+            mbar_arrive_expect_tx(q_full, (uint32_t)(nqt * C::Q_B));
+            for (int q = 0; q < nqt; q++)
+#pragma unroll
+                for (int b = 0; b < HD / 64; b++)
+                    tma_load_3d(smem + C::OFF_Q + q * C::Q_B + b * C::QBOX, &tmq, b * 64, kvh * a.G, t0 + q * QPT, q_full);
+        }
         if (lane < 2 && n > 0) {
             const bool is_v = lane == 1;
             uint64_t* fullx = is_v ? full_v : full_k;
@@ -439,85 +568,58 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
             for (int i = max(0, issued - C::NS); i < issued; i++)
                 mbar_wait(&fullx[i % C::NS], (i / C::NS) & 1, a.err);
         }
+        // never leave the Q copy in flight either (a CTA without keys does not wait for it otherwise)
+        if (lane == 0 && a.q_tma) mbar_wait(q_full, 0, a.err);
     } else {
         // ============================ MMA issuer
         if (lane == 0 && n > 0) {
             const uint32_t idesc_s = umma_idesc(128, C::BN, 0, 0);
             const uint32_t idesc_o = umma_idesc(128, HD, 0, 1);
             const uint32_t q_base = smem_u32(smem + C::OFF_Q);
-            const uint32_t p_base = smem_u32(smem + C::OFF_P);
-            auto issue_s = [&](int i) {          // S(i) = Q K(i)^T into buffer i & 1
+            auto issue_s = [&](int i) {          // S(i) = Q K(i)^T into buffer i & 1 of every live Q tile
                 const uint32_t k_base = smem_u32(smem + C::OFF_ST + (i % C::NS) * C::STAGE_B);
+                for (int q = 0; q < nqt; q++) {
 #pragma unroll
-                for (int kk = 0; kk < HD / 16; kk++) {
-                    const uint64_t ad = umma_desc(q_base + (kk / 4) * C::QBOX + (kk % 4) * 32, 16, 1024);
-                    const uint64_t bd = umma_desc(k_base + (kk / 4) * C::KBOX + (kk % 4) * 32, 16, 1024);
-                    umma_f16(tmem + (i & 1) * C::BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < HD / 16; kk++) {
+                        const uint64_t ad = umma_desc(q_base + q * C::Q_B + (kk / 4) * C::QBOX + (kk % 4) * 32, 16, 1024);
+                        const uint64_t bd = umma_desc(k_base + (kk / 4) * C::KBOX + (kk % 4) * 32, 16, 1024);
+                        umma_f16(tmem + q * C::QCOLS + (i & 1) * C::BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&s_full[2 * q + (i & 1)]);
                 }
-                umma_commit(&s_full[i & 1]);
-                umma_commit(&empty_k[i % C::NS]);   // the K stage is free once S(i) has completed
+                umma_commit(&empty_k[i % C::NS]);   // the K stage is free once every S(i) has completed
             };
             bool ok = wait_or_abort(q_full, 0, a.err, abort_flag);
             if (ok) ok = wait_or_abort(&full_k[0], 0, a.err, abort_flag);
             tc_fence_after();
             if (ok) issue_s(0);
             for (int i = 0; ok && i < n; i++) {
-                // S(i+1) overlaps the softmax of tile i (its buffer held S(i-1), already consumed)
+                // S(i+1) overlaps the softmax of tile i (its buffer held S(i-1), whose P.V was issued)
                 if (i + 1 < n) {
                     const int s1 = (i + 1) % C::NS;
                     if (!wait_or_abort(&full_k[s1], ((i + 1) / C::NS) & 1, a.err, abort_flag)) break;
                     tc_fence_after();
                     issue_s(i + 1);
                 }
-                if (!wait_or_abort(p_full, i & 1, a.err, abort_flag)) break;
                 if (!wait_or_abort(&full_v[i % C::NS], (i / C::NS) & 1, a.err, abort_flag)) break;
-                tc_fence_after();
                 const uint32_t v_base = smem_u32(smem + C::OFF_ST + (i % C::NS) * C::STAGE_B) + C::KV_B;
-                const uint32_t pb = p_base + (i & 1) * C::P_B;
+                for (int q = 0; q < nqt && ok; q++) {
+                    if (!wait_or_abort(&p_full[2 * q + (i & 1)], (i >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t p_tmem = tmem + q * C::QCOLS + (i & 1) * C::BN;   // f16 P: 8 columns per 16 keys
 #pragma unroll
-                for (int kk = 0; kk < C::BN / 16; kk++) {
-                    const uint64_t ad = umma_desc(pb + kk * 32, 16, 1024);
-                    const uint64_t bd = umma_desc(v_base + kk * 16 * 128, C::KBOX, 1024);
-                    umma_f16(tmem + C::OCOL, ad, bd, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < C::BN / 16; kk++) {
+                        const uint64_t bd = umma_desc(v_base + kk * 16 * 128, C::KBOX, 1024);
+                        umma_f16_ts(tmem + q * C::QCOLS + 128, p_tmem + kk * 8, bd, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&o_done[2 * q + (i & 1)]);
                 }
-                umma_commit(&o_done[i & 1]);
+                if (!ok) break;
                 umma_commit(&empty_v[i % C::NS]);
             }
         }
     }
 
-    if (ns > 1) {
-        // ============================ cluster merge of the splits (all 192 threads of every CTA)
-        __syncwarp();
-        cluster_sync_all();
-        const uint32_t rank = cluster_ctarank();
-        const float* po = reinterpret_cast<const float*>(smem + C::OFF_PO);
-        const float* pm = reinterpret_cast<const float*>(smem + C::OFF_PM);
-        // rows [r0, r1) of the tile are merged by this CTA
-        const int r0 = (int)(128 * rank / ns), r1 = (int)(128 * (rank + 1) / ns);
-        constexpr int G4 = HD / 4;
-        for (int gi = threadIdx.x; gi < (r1 - r0) * G4; gi += kPThreads) {
-            const int r = r0 + gi / G4, cc = (gi % G4) * 4;
-            const int qi = r / a.G, g = r % a.G;
-            if (qi >= nq) continue;
-            float M = -INFINITY;
-            for (int sp = 0; sp < ns; sp++) M = fmaxf(M, dsmem_ld_f2(dsmem_map(smem_u32(&pm[r * 2]), sp)).x);
-            float L = 0.0f;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sp = 0; sp < ns; sp++) {
-                const float2 ml = dsmem_ld_f2(dsmem_map(smem_u32(&pm[r * 2]), sp));
-                if (ml.x == -INFINITY) continue;
-                const float w = fast_exp2(ml.x - M);
-                const float4 v = dsmem_ld_f4(dsmem_map(smem_u32(&po[r * HD + cc]), sp));
-                L += ml.y * w;
-                acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
-            }
-            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            float* orow = a.out + (size_t)(t0 + qi) * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
-            *reinterpret_cast<float4*>(orow + cc) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-        }
-        cluster_sync_all();          // every CTA's partial stays valid until all merges read it
-    }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -526,28 +628,29 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     }
 }
 
-template <int HD>
+template <int HD, int NQT>
 cudaError_t prepare_t() {
     static cudaError_t status = [] {
-        using C = PreCfg<HD>;
-        cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        using C = PreCfg<HD, NQT>;
+        cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              C::SMEM + 1024);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fa_prefill_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         return e;
     }();
     return status;
 }
 
-// Splits of the key range per query tile: the fewest that make the CTA count fill whole waves
-// of the SMs best (one CTA per SM), at most 8 per cluster and at least 2 tiles per split.
-int pick_splits(int base_ctas, int min_tiles) {
+// Splits of the key range per CTA (one CTA per SM, no clusters): minimise (waves) x (per-CTA
+// tiles + a merge cost of ~6 tiles when split), at most 8 splits and at least 2 tiles each,
+// within the workspace (partials) and ticket capacity.
+int pick_splits(int units, int tiles, size_t per_split_floats, size_t ws_floats, int n_tickets) {
     int best = 1;
     double best_t = 1e30;
     for (int s = 1; s <= 8; s++) {
-        if (s > 1 && min_tiles / s < 2) break;
-        const double waves = std::ceil((double)base_ctas * s / kNumSMs);
-        const double t = waves / s;
+        if (s > 1 && (tiles / s < 2 || (size_t)units * s * per_split_floats > ws_floats || 2 * units > n_tickets)) break;
+        const double waves = std::ceil((double)units * s / kNumSMs);
+        const double t = waves * ((double)tiles / s + (s > 1 ? 6.0 : 0.0));
         if (t < best_t - 1e-9) {
             best_t = t;
             best = s;
@@ -556,21 +659,40 @@ int pick_splits(int base_ctas, int min_tiles) {
     return best;
 }
 
-template <int HD>
-cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensorMap* tv, cudaStream_t st) {
-    using C = PreCfg<HD>;
-    cudaError_t e = prepare_t<HD>();
+template <int HD, int NQT>
+cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensorMap* tv, float* ws,
+                     size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st) {
+    using C = PreCfg<HD, NQT>;
+    cudaError_t e = prepare_t<HD, NQT>();
     if (e != cudaSuccess) return e;
     AttnArgs a = a_in;
     const int QPT = 128 / a.G;
-    const int n_qtiles = ceil_div(a.T, QPT);
-    // the first query tile sees the fewest keys: size the splits by it
-    const int cb = a.causal_base;                       // host value (device-side bases use max keys)
-    const int min_keys = a.causal_base_dev ? a.S : std::min(a.S, cb + std::min(QPT, a.T));
-    a.n_splits = pick_splits(n_qtiles * a.NKV, (min_keys + C::BN - 1) / C::BN);
-    dim3 grid((unsigned)a.n_splits, (unsigned)n_qtiles, (unsigned)a.NKV);
-    return launch_pdl_cluster(fa_prefill_kernel<HD>, grid, dim3(kPThreads), (size_t)(C::SMEM + 1024), st,
-                              a.n_splits, *tk, *tv, a);
+    const int n_cta_q = ceil_div(a.T, NQT * QPT);
+    const int units = n_cta_q * a.NKV;
+    // key tiles of a typical CTA (host value of the causal base; a device-side base uses max keys)
+    const int keys = a.causal_base_dev ? a.S : std::min(a.S, a.causal_base + std::min(NQT * QPT, a.T));
+    const size_t per_split = (size_t)C::ROWS * (HD + 2);
+    a.n_splits = (ws && tickets) ? pick_splits(units, (keys + C::BN - 1) / C::BN, per_split, ws_floats, n_tickets) : 1;
+    a.cluster_merge = 0;
+    if (a.n_splits > 1) {
+        a.ws_o = ws;
+        a.ws_ml = ws + (size_t)units * a.n_splits * C::ROWS * HD;
+        a.tickets = tickets;
+    }
+    // f16 queries: a 3D map over [T][NH][HD] whose {64, G, QPT} box is one 64-column slab of a Q tile
+    CUtensorMap tq;
+    memset(&tq, 0, sizeof(tq));
+    a.q_tma = 0;
+    if (a.q_type == SV_TYPE_F16) {
+        const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)a.NH, (uint64_t)a.T};
+        const uint64_t strides[2] = {(uint64_t)a.q_nb_h, (uint64_t)a.q_nb_t};
+        const uint32_t box[3] = {64u, (uint32_t)a.G, (uint32_t)QPT};
+        a.q_tma = encode_tmap_3d(&tq, a.q, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B) ? 1 : 0;
+    }
+    dim3 grid((unsigned)a.n_splits, (unsigned)n_cta_q, (unsigned)a.NKV);
+    return launch_pdl(fa_prefill_kernel<HD, NQT>, grid, dim3(C::THREADS), (size_t)(C::SMEM + 1024), st, *tk, *tv,
+                      tq, a);
 }
 
 }  // namespace
@@ -583,13 +705,16 @@ bool prefill_supported(int head_dim, int kv_type, int G, size_t row_bytes) {
 bool make_prefill_tmap(CUtensorMap* m, const void* base, int head_dim, int n_kv_head, size_t row_bytes,
                        int64_t n_rows) {
     return encode_tmap_2d(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, (uint64_t)n_kv_head * head_dim, (uint64_t)n_rows,
-                          row_bytes, 64, PreCfg<128>::BN, CU_TENSOR_MAP_SWIZZLE_128B);
+                          row_bytes, 64, PreCfg<128, 1>::BN, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
-                           cudaStream_t st) {
-    if (head_dim == 128) return launch_t<128>(a, tk, tv, st);
-    if (head_dim == 256) return launch_t<256>(a, tk, tv, st);
+cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv, float* ws,
+                           size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st) {
+    // two query tiles per CTA when the chunk has them (each K/V tile then feeds 256 query rows)
+    if (head_dim == 128)
+        return a.T * a.G > 128 ? launch_t<128, 2>(a, tk, tv, ws, ws_floats, tickets, n_tickets, st)
+                               : launch_t<128, 1>(a, tk, tv, ws, ws_floats, tickets, n_tickets, st);
+    if (head_dim == 256) return launch_t<256, 1>(a, tk, tv, ws, ws_floats, tickets, n_tickets, st);
     return cudaErrorInvalidValue;
 }
 

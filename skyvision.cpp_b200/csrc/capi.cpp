@@ -365,7 +365,8 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     if (kvh) kvh->rows_written_last = false;
     // chunked prefill on the tensor-core kernel when it applies
     if (!window && tkp && tvp && a.mask_mode == SV_MASK_CAUSAL && a.T * a.G > 16) {
-        return cuda_status(launch_prefill(a, head_dim, tkp, tvp, st));
+        return cuda_status(launch_prefill(a, head_dim, tkp, tvp, ws, ws ? ws_bytes / sizeof(float) : 0, tickets,
+                                          tickets ? n_tickets : 0, st));
     }
     const size_t ws_floats = ws ? ws_bytes / sizeof(float) : 0;
     // grouped-query decode (one query tile of <= 8 rows per kv head) on the swap-AB kernel

@@ -65,6 +65,7 @@ struct AttnArgs {
     uint8_t* kc_w;
     uint8_t* vc_w;
     size_t cache_row_bytes;
+    int q_tma;              // prefill kernel: the query tiles arrive by TMA (f16 queries)
     // the fused append may fill its K/V ring before the grid dependency resolves: the launch before
     // it on the stream wrote no cache rows while letting it start early (host-tracked per handle)
     int ring_prefill;
@@ -122,8 +123,8 @@ cudaError_t launch_decode(const AttnArgs& a, int head_dim, int kv_type, const CU
 bool prefill_supported(int head_dim, int kv_type, int G, size_t row_bytes);
 bool make_prefill_tmap(CUtensorMap* m, const void* base, int head_dim, int n_kv_head, size_t row_bytes,
                        int64_t n_rows);
-cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
-                           cudaStream_t st);
+cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv, float* ws,
+                           size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st);
 
 cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
                             const void* src, int src_type, size_t src_nb1, int64_t n_rows,
