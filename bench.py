@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", default="svkv", choices=["svkv", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-5 multi-session leg")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="longctx: how each layer's head outputs reach every rank")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx", "kernels"],
                     help="cfg2: the headline line; longctx: one 131072-token session sharded by kv head; "
                          "kernels: one small launch set of every kernel (for ncu captures)")
@@ -821,9 +823,12 @@ def run_kernels(args):
 
 def run_longctx(args, world, rank, local):
     """One 131072-token session (config-5 long-context run) sharded by KV head: rank g keeps kv heads
-    [g*8/G, (g+1)*8/G) of all 36 layers and their query heads; per layer the fused append + attention
-    kernel runs on the local heads, then NCCL all-gathers the head outputs over NVLink.  Strong
-    scaling: the session's work is fixed, value = decode tokens/s of that session."""
+    [g*8/G, (g+1)*8/G) of all 36 layers and their query heads.  Per layer one kernel appends, attends
+    on the local heads and stores its output rows straight into every rank's gathered buffer over
+    NVLink (peer memory, counted on every rank's arrival counter); the next layer's kernel waits for
+    the previous layer's count before it reads its query rows (`--gather nccl`: attention, then an
+    NCCL all-gather per layer).  Strong scaling: the session's work is fixed, value = decode tokens/s
+    of that session."""
     import importlib
     import torch
     import torch.distributed as dist
@@ -852,12 +857,31 @@ def run_longctx(args, world, rank, local):
         out_l = torch.empty(L, 1, nh_l, HD, dtype=torch.float32, device=dev)
         out_f = torch.empty(L, 1, NH, HD, dtype=torch.float32, device=dev)
         max_keys = S0 + K + W + 1
+        peer = None
+        if args.gather == "peer":
+            peer = sv.Peer(local, rank, world, L, NH * HD * 4)
+            mine = peer.export()
+            if world > 1:
+                handles = [None] * world
+                dist.all_gather_object(handles, mine)
+            else:
+                handles = [mine]
+            peer.import_handles(handles)
+            epoch = torch.ones(1, dtype=torch.int32, device=dev)    # steps count from 1, never rewound
+            barrier(world)
 
         def step():
-            for layer in range(L):
-                kv.attn_append_at(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE, out=out_l[layer],
-                                  stream=stream)
-                hs.gather(out_l[layer], out_f[layer])
+            if peer is None:
+                for layer in range(L):
+                    kv.attn_append_at(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE,
+                                      out=out_l[layer], stream=stream)
+                    hs.gather(out_l[layer], out_f[layer])
+            else:
+                for layer in range(L):
+                    kv.attn_append_at_peer(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE, peer,
+                                           hs.q_lo, NH, layer, layer - 1, epoch, stream=stream)
+                peer.wait(L - 1, epoch, nkv_l * world, err=None, stream=stream)
+                sv.counter_add(epoch, 1, stream=stream)
             sv.counter_add(npast, 1, stream=stream)
 
         step()
@@ -869,7 +893,8 @@ def run_longctx(args, world, rank, local):
             with torch.cuda.graph(g, stream=stream):
                 step()
             run = g.replay
-            how = "one CUDA graph per step (attention kernels + NCCL all-gathers)"
+            how = ("one CUDA graph per step (attention kernels + NCCL all-gathers)" if peer is None else
+                   "one CUDA graph per step (attention kernels storing into every rank's gathered buffer)")
         except Exception as ex:         # capture of the collective unavailable: eager steps
             g = None
             torch.cuda.synchronize()
@@ -890,8 +915,26 @@ def run_longctx(args, world, rank, local):
         barrier(world)
         ms = e0.elapsed_time(e1)
         check_flags(kv, stream)
+        # the gathered rows of the last layer against this rank's own attention of the same step
+        gather_err = None
+        if peer is not None:
+            npast.fill_(S0)
+            torch.cuda.synchronize()
+            barrier(world)
+            step()
+            stream.synchronize()
+            barrier(world)
+            got = peer.slot(L - 1, (1, NH, HD))[:, hs.q_lo:hs.q_hi].clone()
+            npast.fill_(S0)
+            kv.attn_at(L - 1, ql[L - 1], npast, max_keys, SCALE, out=out_l[L - 1], stream=stream)
+            stream.synchronize()
+            gather_err = float((got - out_l[L - 1]).abs().max().item())
+            check_flags(kv, stream)
     ms_max = max_over_ranks(ms, world)
     del g
+    if peer is not None:
+        barrier(world)
+        peer.free()
     kv.free()
     if rank != 0:
         return
@@ -905,7 +948,10 @@ def run_longctx(args, world, rank, local):
         "dtype": "f16", "data": "synthetic",
         "config": {"workload": "one session of 131072 cached rows, 36 layers, 32q/8kv HD 128 f16 "
                                f"({nkv_l} kv heads per GPU)", "step": how,
-                   "parallelism": f"kv-head sharding over {world} GPU(s), NCCL all-gather of head outputs per layer"},
+                   "parallelism": f"kv-head sharding over {world} GPU(s), " + (
+                       "NCCL all-gather of head outputs per layer" if args.gather == "nccl" else
+                       "head outputs stored into every rank's buffer by the attention kernel (NVLink peer memory)")},
+        "gather_check_max_abs": gather_err,
         "kv_gbs": step_bytes / (ms_max / K * 1e-3) / 1e9,
         "kv_gbs_per_gpu": step_bytes / world / (ms_max / K * 1e-3) / 1e9,
         "hbm_frac_per_gpu": step_bytes / world / (ms_max / K * 1e-3) / 1e9 / hbm,

@@ -266,6 +266,37 @@ int sv_session_end_turn(sv_session* s, int frames, int text_rows, int answer_row
  * compacted) row id of cache row i, i < *n_rows (max_rows caps the copy). */
 int sv_session_rows(const sv_session* s, int* n_rows, int64_t* rows_out, int max_rows);
 
+/* ---------------------------------------------------------------- head-sharded decode, gather fused in
+ * One session too long for one GPU's bandwidth shards by kv head (rank g holds kv heads
+ * [g*NKV/G, (g+1)*NKV/G) and their query heads).  The reference-side design gathers each layer's
+ * [T, NH/G, HD] outputs with an all-gather after attention; here the attention kernel's output
+ * stores go straight into every rank's gathered buffer over NVLink (CUDA IPC peer memory) and count
+ * themselves on every rank's arrival counter.  No reference counterpart (the reference runs one
+ * process per model, qwen3vl_model.cpp:657-663); replaces the NCCL all-gather of this build's
+ * sharded decode.
+ *
+ * sv_peer_create allocates this rank's gathered buffer (n_slots regions of slot_bytes, one per
+ * layer, rows [T][n_head_total][HD] f32) and its counters; sv_peer_export writes its IPC handle
+ * (SV_PEER_HANDLE_BYTES); after exchanging handles (any host channel), sv_peer_import opens every
+ * rank's buffer (handles in rank order).  sv_attn_append_at_peer is sv_attn_append_at for this
+ * rank's n_head heads whose output rows land at head_offset of slot `slot` on every rank; when
+ * wait_slot >= 0 it first waits (bounded, on the device) until slot wait_slot holds the current
+ * epoch's rows from every rank (the previous layer's gather).  *epoch_dev counts steps from 1 and is
+ * advanced by the caller after each step (sv_counter_add).  sv_peer_wait is that wait alone.
+ * f16 caches, head_dim 64/128, T * (n_head / n_kv_head) <= 8; otherwise SV_ERR_UNSUPPORTED. */
+#define SV_PEER_HANDLE_BYTES 64
+typedef struct sv_peer sv_peer;
+int sv_peer_create(int device, int rank, int world, int n_slots, size_t slot_bytes, sv_peer** out);
+int sv_peer_export(const sv_peer* p, void* handle);
+int sv_peer_import(sv_peer* p, const void* handles);
+int sv_peer_slot(const sv_peer* p, int slot, void** data);
+int sv_peer_wait(sv_peer* p, int slot, const int32_t* epoch_dev, int per_epoch, int* err_dev, void* stream);
+int sv_peer_destroy(sv_peer* p);
+int sv_attn_append_at_peer(sv_kv* kv, int layer, const void* q, int q_type, const void* k_new, const void* v_new,
+                           int T, int n_head, const int32_t* n_past_dev, int max_keys, float scale, sv_peer* peer,
+                           int head_offset, int n_head_total, int slot, int wait_slot, const int32_t* epoch_dev,
+                           void* stream);
+
 /* ================================================================ failure detection
  * Every on-device wait of the library is bounded; on expiry the kernel sets
  * SV_DEVERR_TIMEOUT in its error word and unwinds instead of hanging.  This

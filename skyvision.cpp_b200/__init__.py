@@ -26,6 +26,8 @@ import os
 import re
 import subprocess
 
+import numpy as np
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libsvkv.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "svkv.h")
@@ -112,6 +114,13 @@ def lib() -> ctypes.CDLL:
         "sv_session_end_turn": (I, [P, I, I, I]),
         "sv_session_rows": (I, [P, ctypes.POINTER(I), P, I]),
         "sv_selftest_wait_timeout": (I, [P, P, ctypes.c_uint, P]),
+        "sv_peer_create": (I, [I, I, I, I, SZ, ctypes.POINTER(P)]),
+        "sv_peer_export": (I, [P, P]),
+        "sv_peer_import": (I, [P, P]),
+        "sv_peer_slot": (I, [P, I, ctypes.POINTER(P)]),
+        "sv_peer_wait": (I, [P, I, P, I, P, P]),
+        "sv_peer_destroy": (I, [P]),
+        "sv_attn_append_at_peer": (I, [P, I, P, I, P, P, I, I, P, I, F, P, I, I, I, I, P, P]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -220,6 +229,18 @@ class KvCache:
         _check("sv_kv_append_at", lib().sv_kv_append_at(self.h, layer, _ptr(k), _ptr(v), st, k.shape[0],
                                                         _ptr(base_dev), _stream(stream)))
 
+    def attn_append_at_peer(self, layer: int, q, k_new, v_new, n_past_dev, max_keys: int, scale: float, peer,
+                            head_offset: int, n_head_total: int, slot: int, wait_slot: int, epoch_dev, stream=None):
+        """attn_append_at for this rank's heads with the gather fused in: the output rows land at
+        head_offset of `peer` slot `slot` on every rank (see Peer)."""
+        import torch
+        T, NH, HD = q.shape
+        qt = TYPE_F32 if q.dtype == torch.float32 else TYPE_F16
+        _check("sv_attn_append_at_peer",
+               lib().sv_attn_append_at_peer(self.h, layer, _ptr(q), qt, _ptr(k_new), _ptr(v_new), T, NH,
+                                            _ptr(n_past_dev), max_keys, scale, peer.h, head_offset, n_head_total,
+                                            slot, wait_slot, _ptr(epoch_dev), _stream(stream)))
+
     def attn_at(self, layer: int, q, n_past_dev, max_keys: int, scale: float, out=None, stream=None):
         """attn with n_past read on the device (graph-capturable)."""
         import torch
@@ -277,6 +298,56 @@ class KvCache:
         f = ctypes.c_int()
         _check("sv_kv_error", lib().sv_kv_error(self.h, ctypes.byref(f), _stream(stream)))
         return f.value
+
+
+PEER_HANDLE_BYTES = 64
+
+
+class Peer:
+    """Gathered-output buffers of a head-sharded session shared across ranks (sv_peer_*).
+
+    p = Peer(device, rank, world, n_slots, slot_bytes); handles = all ranks' p.export() (any host
+    channel, e.g. torch.distributed.all_gather_object); p.import_handles(handles); then
+    KvCache.attn_append_at_peer(...) per layer and p.slot(s) views the gathered rows."""
+
+    def __init__(self, device: int, rank: int, world: int, n_slots: int, slot_bytes: int):
+        h = ctypes.c_void_p()
+        _check("sv_peer_create", lib().sv_peer_create(device, rank, world, n_slots, slot_bytes, ctypes.byref(h)))
+        self.h, self.device, self.rank, self.world = h.value, device, rank, world
+        self.n_slots, self.slot_bytes = n_slots, slot_bytes
+
+    def export(self) -> bytes:
+        buf = (ctypes.c_char * PEER_HANDLE_BYTES)()
+        _check("sv_peer_export", lib().sv_peer_export(self.h, buf))
+        return bytes(buf)
+
+    def import_handles(self, handles) -> None:
+        blob = b"".join(handles)
+        assert len(blob) == PEER_HANDLE_BYTES * self.world
+        buf = (ctypes.c_char * len(blob)).from_buffer_copy(blob)
+        _check("sv_peer_import", lib().sv_peer_import(self.h, buf))
+
+    def slot(self, s: int, shape=None):
+        """torch f32 view of slot s (shape defaults to the whole slot, flat)."""
+        import torch
+        p = ctypes.c_void_p()
+        _check("sv_peer_slot", lib().sv_peer_slot(self.h, s, ctypes.byref(p)))
+        t = device_view(p.value, self.slot_bytes, self.device).view(torch.float32)
+        return t if shape is None else t[: int(np.prod(shape))].view(*shape)
+
+    def wait(self, s: int, epoch_dev, per_epoch: int, err=None, stream=None) -> None:
+        _check("sv_peer_wait", lib().sv_peer_wait(self.h, s, _ptr(epoch_dev), per_epoch, _ptr(err), _stream(stream)))
+
+    def free(self) -> None:
+        if self.h:
+            lib().sv_peer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
 
 
 def counter_add(counter, delta: int, stream=None) -> None:

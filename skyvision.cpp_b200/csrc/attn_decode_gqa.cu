@@ -69,7 +69,7 @@ struct GqaCfg {
     static constexpr int PUSH_ML = 16 * kRows * HD * 4;
     static_assert(PUSH_ML + 16 * kRows * 8 <= RING_B, "merge slots must fit in the stage ring");
     static constexpr int BAR_OFF = RING_B;
-    static constexpr int SMEM = BAR_OFF + (2 * STAGES + 1) * 8 + 16;
+    static constexpr int SMEM = BAR_OFF + (2 * STAGES + 1) * 8 + 16;   // + abort and last-split flags
 };
 
 __device__ __forceinline__ void consumer_sync() {
@@ -95,6 +95,44 @@ __device__ __forceinline__ void st_async_f4(uint32_t caddr, float4 v, uint32_t c
 __device__ __forceinline__ void st_async_f2(uint32_t caddr, float2 v, uint32_t cbar) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];"
                  ::"r"(caddr), "f"(v.x), "f"(v.y), "r"(cbar) : "memory");
+}
+
+// One finished (row, 4-column) group of the output: to `out`, or with the gather fused in, into
+// every rank's gathered buffer over NVLink (plain stores to peer memory).
+__device__ __forceinline__ void store_out4(const AttnArgs& a, int kvh, int r, int c, float4 v) {
+    const int qi = r / a.G, g = r % a.G;
+    if (a.n_peers == 0) {
+        float* orow = a.out + (size_t)qi * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
+        *reinterpret_cast<float4*>(orow + c) = v;
+        return;
+    }
+    for (int p = 0; p < a.n_peers; p++) {   // every rank's gathered buffer, this rank's own included
+        float* prow = a.peer_out[p] + (size_t)qi * a.peer_nb_t + (size_t)(a.head_offset + kvh * a.G + g) * a.out_nb_h;
+        *reinterpret_cast<float4*>(prow + c) = v;
+    }
+}
+
+// After all of a kv head's rows were stored (by the threads that named barrier `bar_id` joins):
+// make them visible system-wide, then count the head on every rank.
+__device__ __forceinline__ void signal_peers(const AttnArgs& a, int bar_id, int n_threads) {
+    if (a.n_peers == 0) return;
+    __threadfence_system();
+    __syncwarp();
+    asm volatile("barrier.sync %0, %1;" ::"r"(bar_id), "r"(n_threads) : "memory");
+    if (threadIdx.x == 0)
+        for (int p = 0; p < a.n_peers; p++) atomicAdd_system(a.peer_ctr[p], 1u);
+}
+
+// Wait (bounded) for the previous layer's gather: *wait_ctr >= *epoch * per_epoch.
+__device__ __forceinline__ void wait_gather(const AttnArgs& a) {
+    const unsigned int target = (unsigned int)(*reinterpret_cast<const volatile int*>(a.epoch_dev)) * a.wait_per_epoch;
+    const uint64_t t0 = globaltimer_ns();
+    while (*reinterpret_cast<const volatile unsigned int*>(a.wait_ctr) < target) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (a.err) atomicOr(a.err, ERRBIT_TIMEOUT);
+            break;
+        }
+    }
 }
 
 template <int HD>
@@ -144,35 +182,35 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         const int gi = threadIdx.x, n_gm = R * G4m;
         pdl_wait();   // the output may still be in use by the previous launch
         if (threadIdx.x == 0) pdl_trigger();   // the splits decide when the next launch may start
-        if (gi >= n_gm) return;
-        if (!mbar_wait(mdata, 0, a.err)) return;
-        const int r = gi / G4m, c = (gi % G4m) * 4;
-        const float* slot_o = reinterpret_cast<const float*>(smem + C::PUSH_O);
-        const float* slot_ml = reinterpret_cast<const float*>(smem + C::PUSH_ML);
-        const int ns = a.n_splits;
-        float2 ml[16];
+        // every thread reaches the final signal (a named barrier when the gather is fused in)
+        if (gi < n_gm && mbar_wait(mdata, 0, a.err)) {
+            const int r = gi / G4m, c = (gi % G4m) * 4;
+            const float* slot_o = reinterpret_cast<const float*>(smem + C::PUSH_O);
+            const float* slot_ml = reinterpret_cast<const float*>(smem + C::PUSH_ML);
+            const int ns = a.n_splits;
+            float2 ml[16];
 #pragma unroll
-        for (int sp = 0; sp < 16; sp++)
-            if (sp < ns) ml[sp] = *reinterpret_cast<const float2*>(&slot_ml[(sp * kRows + r) * 2]);
-        float MM = -INFINITY;
+            for (int sp = 0; sp < 16; sp++)
+                if (sp < ns) ml[sp] = *reinterpret_cast<const float2*>(&slot_ml[(sp * kRows + r) * 2]);
+            float MM = -INFINITY;
 #pragma unroll
-        for (int sp = 0; sp < 16; sp++)
-            if (sp < ns) MM = fmaxf(MM, ml[sp].x);
-        float LL = 0.0f;
-        float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sp = 0; sp < 16; sp++)
+                if (sp < ns) MM = fmaxf(MM, ml[sp].x);
+            float LL = 0.0f;
+            float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int sp = 0; sp < 16; sp++) {
-            if (sp < ns && ml[sp].x != -INFINITY) {
-                const float w = fast_exp2(ml[sp].x - MM);
-                LL += ml[sp].y * w;
-                const float4 v = *reinterpret_cast<const float4*>(&slot_o[(sp * kRows + r) * HD + c]);
-                o4.x += v.x * w; o4.y += v.y * w; o4.z += v.z * w; o4.w += v.w * w;
+            for (int sp = 0; sp < 16; sp++) {
+                if (sp < ns && ml[sp].x != -INFINITY) {
+                    const float w = fast_exp2(ml[sp].x - MM);
+                    LL += ml[sp].y * w;
+                    const float4 v = *reinterpret_cast<const float4*>(&slot_o[(sp * kRows + r) * HD + c]);
+                    o4.x += v.x * w; o4.y += v.y * w; o4.z += v.z * w; o4.w += v.w * w;
+                }
             }
+            const float inv = LL > 0.0f ? 1.0f / LL : 0.0f;
+            store_out4(a, kvh, r, c, make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv));
         }
-        const float inv = LL > 0.0f ? 1.0f / LL : 0.0f;
-        const int qi = r / a.G, g = r % a.G;
-        float* orow = a.out + (size_t)qi * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
-        *reinterpret_cast<float4*>(orow + c) = make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv);
+        signal_peers(a, 3, kThreads);
         return;
     }
 
@@ -239,6 +277,13 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     }
     pdl_wait();
 
+    // with the gather fused in, the query rows may depend on the previous layer's gathered output:
+    // thread 0 waits (bounded) for its arrival count, then the consumer warps go on
+    if (a.wait_ctr && warp < kCWarps) {
+        if (threadIdx.x == 0) wait_gather(a);
+        __syncwarp();
+        asm volatile("barrier.sync 1, %0;" ::"n"(kCThreads) : "memory");
+    }
     // consumers: the query rows first (nothing below waits on them until the first tile)
     const int gq = lane >> 2, tq = lane & 3;     // fragment row / column-pair index
     const int q_es = a.q_type == SV_TYPE_F32 ? 4 : 2;
@@ -468,7 +513,7 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 
     constexpr int G4 = HD / 4;
     const int n_g = R * G4;
-    if (!a.cluster_merge) {   // one split: normalise and store
+    if (!a.cluster_merge && a.n_splits == 1) {   // one split: normalise and store
         for (int gi = tid; gi < n_g; gi += kCThreads) {
             const int r = gi / G4, c = (gi % G4) * 4;
             float M = -INFINITY;
@@ -485,10 +530,104 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
             }
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            const int qi = r / a.G, g = r % a.G;
-            float* orow = a.out + (size_t)qi * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
-            *reinterpret_cast<float4*>(orow + c) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+            store_out4(a, kvh, r, c, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
         }
+        signal_peers(a, 1, kCThreads);
+        return;
+    }
+
+    if (!a.cluster_merge) {
+        // ---- split-K without a cluster (many splits: few kv heads over a long context): every
+        // split publishes its partial to the workspace, and the last CTA of the kv head (atomic
+        // ticket, no spinning) merges all partials and resets the ticket.
+        volatile int* last = flag + 1;
+        const int ns = a.n_splits;
+        const size_t pbase = ((size_t)kvh * ns + split) * 16;   // 16-row partial slots per split
+        for (int gi = tid; gi < n_g; gi += kCThreads) {
+            const int r = gi / G4, c = (gi % G4) * 4;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kCWarps; w++) M = fmaxf(M, cm[w * kRows + r]);
+            float L = 0.0f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int w = 0; w < kCWarps; w++) {
+                const float mw = cm[w * kRows + r];
+                const float sc = mw == -INFINITY ? 0.0f : fast_exp2(mw - M);
+                L += cl[w * kRows + r] * sc;
+                const float4 v = *reinterpret_cast<const float4*>(&cw[(w * kRows + r) * C::CW_LD + c]);
+                acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
+            }
+            *reinterpret_cast<float4*>(&a.ws_o[(pbase + r) * HD + c]) = acc;
+            if (c == 0) *reinterpret_cast<float2*>(&a.ws_ml[(pbase + r) * 2]) = make_float2(M, L);
+        }
+        __threadfence();
+        consumer_sync();
+        if (tid == 0) *last = atomicAdd(&a.tickets[kvh], 1) == ns - 1;
+        consumer_sync();
+        if (!*last) return;
+        __threadfence();
+        // per (row, split) weights exp2(m_s - M) / L into shared memory (the combine scratch is free)
+        float* wgt = reinterpret_cast<float*>(smem);           // [kRows][ns]
+        const size_t tbase = (size_t)kvh * ns * 16;
+        for (int r = warp; r < R; r += kCWarps) {
+            float M = -INFINITY;
+            for (int sp = lane; sp < ns; sp += 32) M = fmaxf(M, __ldcg(&a.ws_ml[(tbase + (size_t)sp * 16 + r) * 2]));
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+            float L = 0.0f;
+            for (int sp = lane; sp < ns; sp += 32) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(&a.ws_ml[(tbase + (size_t)sp * 16 + r) * 2]));
+                const float w = ml.x == -INFINITY ? 0.0f : fast_exp2(ml.x - M);
+                wgt[r * ns + sp] = w;
+                L += ml.y * w;
+            }
+#pragma unroll
+            for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            __syncwarp();
+            for (int sp = lane; sp < ns; sp += 32) wgt[r * ns + sp] *= inv;
+        }
+        consumer_sync();
+        // n_g (row, 4-column) groups over the 256 consumer threads: P threads per group, each summing
+        // every P-th split with eight loads in flight, then the P partial sums meet in shared memory
+        const int P = max(1, kCThreads / n_g);
+        float4* part = reinterpret_cast<float4*>(smem + ((R * ns * 4 + 15) & ~15));   // [P][n_g]
+        if (tid < P * n_g) {
+            const int gi = tid % n_g, sub = tid / n_g;
+            const int r = gi / G4, c = (gi % G4) * 4;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            int sp = sub;
+            for (; sp + 7 * P < ns; sp += 8 * P) {
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++)
+                    v[u] = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[(tbase + (size_t)(sp + u * P) * 16 + r) * HD + c]));
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const float w = wgt[r * ns + sp + u * P];
+                    acc.x += v[u].x * w; acc.y += v[u].y * w; acc.z += v[u].z * w; acc.w += v[u].w * w;
+                }
+            }
+            for (; sp < ns; sp += P) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[(tbase + (size_t)sp * 16 + r) * HD + c]));
+                const float w = wgt[r * ns + sp];
+                acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+            }
+            part[sub * n_g + gi] = acc;
+        }
+        consumer_sync();
+        for (int gi = tid; gi < n_g; gi += kCThreads) {
+            const int r = gi / G4, c = (gi % G4) * 4;
+            float4 acc = part[gi];
+            for (int sub = 1; sub < P; sub++) {
+                const float4 v = part[sub * n_g + gi];
+                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            store_out4(a, kvh, r, c, acc);
+        }
+        if (tid == 0) a.tickets[kvh] = 0;
+        signal_peers(a, 1, kCThreads);
         return;
     }
 
@@ -578,7 +717,8 @@ int decode_gqa_max_cluster(int head_dim) {
 
 cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
                               cudaStream_t st) {
-    if (a.n_qtiles != 1 || a.T * a.G > kRows || (a.n_splits > 1 && !a.cluster_merge)) return cudaErrorInvalidValue;
+    if (a.n_qtiles != 1 || a.T * a.G > kRows || (a.n_splits > 1 && !a.cluster_merge && !a.tickets))
+        return cudaErrorInvalidValue;
     switch (head_dim) {
         case 64: return launch_gqa_t<64>(a, tk, tv, st);
         case 128: return launch_gqa_t<128>(a, tk, tv, st);

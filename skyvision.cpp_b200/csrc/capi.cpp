@@ -389,7 +389,8 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     } else {
         // per-query windows differ in length (multi-session batches): aim for several waves of
         // CTAs so the short sessions' idle splits do not leave SMs waiting on the long ones
-        const int target = window ? 8 * target_ctas_default() : target_ctas_default();
+        // (the GQA kernel runs two CTAs per SM)
+        const int target = window ? 8 * target_ctas_default() : (gqa ? 2 : 1) * target_ctas_default();
         p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0, target);
         a.cluster_merge = 0;
     }
@@ -397,14 +398,13 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     a.n_qtiles = p.n_qtiles;
     a.chunk = p.chunk;
     a.n_splits = p.n_splits;
-    if (gqa && a.n_qtiles == 1 && (a.n_splits == 1 || a.cluster_merge))
-        return cuda_status(launch_decode_gqa(a, head_dim, tk, tv, st));
     if (a.n_splits > 1 && !a.cluster_merge) {
         const size_t n_part = (size_t)a.NKV * a.n_qtiles * a.n_splits * 16;
         a.ws_o = ws;
         a.ws_ml = ws + n_part * head_dim;
         a.tickets = tickets;
     }
+    if (gqa && a.n_qtiles == 1) return cuda_status(launch_decode_gqa(a, head_dim, tk, tv, st));
     return cuda_status(launch_decode(a, head_dim, kv_type, tk, tv, st));
 }
 
@@ -644,6 +644,64 @@ int sv_flash_attn_ext(const sv_fa_params* p, void* workspace, size_t ws_bytes, v
         }
     }
     return run_attention(nullptr, &tk, &tv, nullptr, nullptr, HD, p->k_type, a, S, false, ws, wsb, tickets, n_tk, st);
+}
+
+int sv_attn_append_at_peer(sv_kv* kv, int layer, const void* q, int q_type, const void* k_new, const void* v_new,
+                           int T, int n_head, const int32_t* n_past_dev, int max_keys, float scale, sv_peer* peer,
+                           int head_offset, int n_head_total, int slot, int wait_slot, const int32_t* epoch_dev,
+                           void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !q || !k_new || !v_new || T <= 0 || n_head <= 0 || !n_past_dev ||
+        max_keys < T || !peer || !peer->imported || !epoch_dev || slot < 0 || slot >= peer->n_slots ||
+        wait_slot >= peer->n_slots || head_offset < 0 || head_offset + n_head > n_head_total)
+        return SV_ERR_INVALID;
+    if (peer->device != kv->device) return SV_ERR_INVALID;
+    if (n_head % kv->n_kv_head != 0) return SV_ERR_UNSUPPORTED;
+    const int G = n_head / kv->n_kv_head;
+    const int HD = kv->head_dim;
+    // the fused gather lives in the grouped-query decode kernel
+    if (!gqa_enabled() || !decode_gqa_applies(HD, kv->type, T, G, SV_MASK_CAUSAL)) return SV_ERR_UNSUPPORTED;
+    if (q_type != SV_TYPE_F16 && q_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    if ((size_t)T * n_head_total * HD * sizeof(float) > peer->slot_bytes) return SV_ERR_INVALID;
+    if (max_keys > kv->n_ctx) return SV_ERR_OVERFLOW;
+    if (kv->tm_dec.empty()) return SV_ERR_UNSUPPORTED;
+    DeviceGuard g(kv->device);
+    const int es = q_type == SV_TYPE_F32 ? 4 : 2;
+    AttnArgs a{};
+    a.q = static_cast<const uint8_t*>(q);
+    a.q_type = q_type;
+    a.q_nb_h = (int64_t)HD * es;
+    a.q_nb_t = (int64_t)n_head * HD * es;
+    a.T = T;
+    a.NH = n_head;
+    a.NKV = kv->n_kv_head;
+    a.G = G;
+    a.S = max_keys;
+    a.mask_mode = SV_MASK_CAUSAL;
+    a.causal_base_dev = n_past_dev;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.out = nullptr;
+    a.out_nb_h = HD;
+    a.out_nb_t = (int64_t)n_head * HD;
+    a.err = kv->err;
+    a.n_new = T;
+    a.knew = static_cast<const uint8_t*>(k_new);
+    a.vnew = static_cast<const uint8_t*>(v_new);
+    a.new_nb_t = (int64_t)kv->n_kv_head * HD * 2;
+    a.kc_w = kv->tensor(layer, 0);
+    a.vc_w = kv->tensor(layer, 1);
+    a.cache_row_bytes = kv->row_bytes;
+    a.peer_out = peer->d_out + (size_t)slot * peer->world;
+    a.peer_ctr = peer->d_ctr + (size_t)slot * peer->world;
+    a.n_peers = peer->world;
+    a.head_offset = head_offset;
+    a.peer_nb_t = (int64_t)n_head_total * HD;
+    a.epoch_dev = epoch_dev;
+    // each rank's output CTAs count once per kv head on every rank
+    a.wait_per_epoch = (unsigned int)(kv->n_kv_head * peer->world);
+    a.wait_ctr = wait_slot >= 0 ? peer->ctr(wait_slot) : nullptr;
+    return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], nullptr, nullptr, HD, kv->type, a,
+                         max_keys, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
+                         static_cast<cudaStream_t>(stream), /*allow_cluster=*/true);
 }
 
 int sv_soft_max_ext(const float* x, int64_t ne0, int64_t n_rows, size_t x_nb1, const void* mask, int64_t mask_rows,

@@ -66,6 +66,20 @@ struct AttnArgs {
     uint8_t* vc_w;
     size_t cache_row_bytes;
     int q_tma;              // prefill kernel: the query tiles arrive by TMA (f16 queries)
+    // Head-sharded decode with the all-gather fused in (GQA decode kernel): every finished output
+    // row is also stored into each rank's gathered buffer (peer_out[p], this slot's region, rows
+    // laid out [T][n_head_total][HD] with this rank's heads at head_offset), and the CTA that
+    // stored a kv head's rows then adds 1 to every rank's arrival counter peer_ctr[p].
+    float* const* peer_out;
+    unsigned int* const* peer_ctr;
+    int n_peers;            // 0: plain output to out
+    int head_offset;
+    int64_t peer_nb_t;      // floats between queries in the gathered buffer
+    // Before reading its query rows, wait (bounded) until *wait_ctr >= *epoch_dev * wait_per_epoch
+    // (the previous layer's gather is complete); wait_ctr == nullptr: no wait.
+    const unsigned int* wait_ctr;
+    const int32_t* epoch_dev;
+    unsigned int wait_per_epoch;
     // the fused append may fill its K/V ring before the grid dependency resolves: the launch before
     // it on the stream wrote no cache rows while letting it start early (host-tracked per handle)
     int ring_prefill;
@@ -144,3 +158,23 @@ cudaError_t launch_soft_max(const float* x, int64_t ne0, int64_t n_rows, size_t 
 }  // namespace svkv
 
 struct sv_kv : svkv::KvHandle {};
+
+namespace svkv {
+// Gathered-output buffers of a head-sharded session, one per rank, mapped into every rank over
+// CUDA IPC (peer memory over NVLink).  Local allocation: n_slots regions of slot_bytes, then one
+// 32-bit arrival counter per slot.
+struct PeerGroup {
+    int device = 0, rank = 0, world = 1, n_slots = 0;
+    size_t slot_bytes = 0, ctr_off = 0, buf_bytes = 0;
+    uint8_t* buf = nullptr;
+    uint8_t* base[8] = {nullptr};      // every rank's buffer in this process (base[rank] = buf)
+    bool opened[8] = {false};
+    float** d_out = nullptr;           // device [n_slots][world]: each rank's region of a slot
+    unsigned int** d_ctr = nullptr;    // device [n_slots][world]: each rank's counter of a slot
+    bool imported = false;
+    unsigned int* ctr(int slot) const { return reinterpret_cast<unsigned int*>(buf + ctr_off) + slot; }
+};
+cudaError_t launch_peer_wait(const unsigned int* ctr, const int32_t* epoch_dev, unsigned int per_epoch, int* err,
+                             cudaStream_t st);
+}  // namespace svkv
+struct sv_peer : svkv::PeerGroup {};

@@ -422,3 +422,29 @@ def test_decode_long_context_back_to_back(orc, fused, NH):
             assert np.array_equal(vc[n0 + i].view(np.uint16), v[layer, 0])
         ref = ref_attn(orc, kv, layer, q[layer], n0 + steps - 1, 1 / np.sqrt(HD))
         close(got[layer], ref)
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_decode_few_kv_heads_long_context(orc, fused):
+    """Few kv heads over a long context (the per-GPU shard of one long session): more key splits
+    than a cluster holds, so the splits merge through the workspace (ticket) path."""
+    NKV, NH, HD, n0 = 1, 4, 128, 30000
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, NKV, HD, n0 + 8)
+    g = torch.Generator(device=DEV)
+    g.manual_seed(41)
+    kv.tensor(0, 0).view(torch.float16)[:n0].normal_(generator=g)
+    kv.tensor(0, 1).view(torch.float16)[:n0].normal_(generator=g)
+    q = orc.normal_f16(41, 1, NH * HD).reshape(1, NH, HD)
+    k = orc.normal_f16(41, 2, NKV * HD).reshape(1, NKV * HD)
+    td = lambda a: torch.from_numpy(a.view(np.float16)).to(DEV)
+    npast = torch.full((1,), n0, dtype=torch.int32, device=DEV)
+    for rep in range(2):                       # a second call reuses the reset tickets
+        if fused:
+            out = kv.attn_append_at(0, td(q), td(k), td(k), npast, n0 + 4, 1 / np.sqrt(HD))
+        else:
+            kv.append(0, td(k), td(k), base=n0)
+            out = kv.attn(0, td(q), n_past=n0, scale=1 / np.sqrt(HD))
+        torch.cuda.synchronize()
+        assert kv.error_flags() == 0
+        close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n0, 1 / np.sqrt(HD)))
