@@ -48,29 +48,48 @@ constexpr int kRows = 8;                   // query rows per kv head (N of the M
 constexpr int kL2Ahead = 4;                // K/V tiles past the ring prefetched into L2 before the wait
 
 
-template <int HD>
+constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+template <int HD, int KVT>
 struct GqaCfg {
+    static constexpr bool Q8 = KVT == SV_TYPE_Q8_0;
     static constexpr int COLS = 64;                       // f16 columns per TMA box (128-byte swizzle span)
     static constexpr int NB = HD / COLS;
     static constexpr int PITCH = COLS * 2;
     static constexpr int BOXB = kBK * PITCH;
-    static constexpr int TILE_B = NB * BOXB;              // K (or V) bytes per tile
-    static constexpr int STAGE_B = 2 * TILE_B;
-    static constexpr int STAGES = HD == 128 ? 3 : 6;      // ~96 KB ring: two CTAs per SM
+    static constexpr int HEADB = Q8 ? HD / kQK8_0 * kQ8_0Bytes : HD * 2;   // one kv head of one cache row
+    static constexpr int TILE_B = Q8 ? kBK * HEADB : NB * BOXB;          // K (or V) bytes per tile
+    static constexpr int STAGE_B = align_up(2 * TILE_B, 1024);
+    // f16 HD 64/128: ~96 KB ring, two CTAs per SM; q8_0 HD 256: one CTA per SM, deeper ring
+    static constexpr int STAGES = Q8 ? 4 : (HD == 128 ? 3 : 6);
+    static constexpr int MIN_BLOCKS = Q8 ? 1 : 2;
+    static constexpr int ROWS_MAX = HD >= 256 ? 4 : kRows;              // query rows per kv head
     static constexpr int RING_B = STAGES * STAGE_B;
     static constexpr int CW_LD = HD + 4;                  // padded row of the warp-combine scratch
     static constexpr int CW_B = kCWarps * kRows * CW_LD * 4;
     static constexpr int CM_OFF = CW_B;                   // [warp][row] maxima, then sums
     static_assert(CM_OFF + 2 * kCWarps * kRows * 4 <= RING_B, "combine scratch must fit in the stage ring");
-    static_assert(kRows * (HD / 4) <= kCThreads, "one (row, 4-column) group per consumer thread");
-    // cluster merge, leader CTA only, written by the other splits once every split has left the ring:
-    // partial O [split][row][HD] and (m, l) [split][row]
+    static_assert(ROWS_MAX * (HD / 4) <= kCThreads, "one (row, 4-column) group per consumer thread");
+    // cluster merge, merger CTA only: partial O [split][row][HD] and (m, l) [split][row]
     static constexpr int PUSH_O = 0;
     static constexpr int PUSH_ML = 16 * kRows * HD * 4;
     static_assert(PUSH_ML + 16 * kRows * 8 <= RING_B, "merge slots must fit in the stage ring");
-    static constexpr int BAR_OFF = RING_B;
+    // q8_0: each consumer warp expands the V rows of its 16 keys into f16 integers here
+    static constexpr int WST_B = Q8 ? 16 * HD * 2 : 0;
+    static constexpr int STG_OFF = RING_B;
+    static constexpr int BAR_OFF = STG_OFF + kCWarps * WST_B;
     static constexpr int SMEM = BAR_OFF + (2 * STAGES + 1) * 8 + 16;   // + abort and last-split flags
+    static_assert(SMEM + 1024 <= 227 * 1024, "shared memory budget");
 };
+
+// two signed bytes (low, high of w) -> exact f16x2 (1024 + (b + 128) - 1152)
+__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w) {
+    const uint32_t lo = (w & 0xffu) ^ 0x80u;
+    const uint32_t hi = ((w >> 8) & 0xffu) ^ 0x80u;
+    const uint32_t h = (0x6400u | lo) | ((0x6400u | hi) << 16);
+    __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x6480u)));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
 
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kCThreads) : "memory");
@@ -99,9 +118,10 @@ __device__ __forceinline__ void st_async_f2(uint32_t caddr, float2 v, uint32_t c
 
 // One finished (row, 4-column) group of the output: to `out`, or with the gather fused in, into
 // every rank's gathered buffer over NVLink (plain stores to peer memory).
+template <bool kPeer>
 __device__ __forceinline__ void store_out4(const AttnArgs& a, int kvh, int r, int c, float4 v) {
     const int qi = r / a.G, g = r % a.G;
-    if (a.n_peers == 0) {
+    if (!kPeer) {
         float* orow = a.out + (size_t)qi * a.out_nb_t + (size_t)(kvh * a.G + g) * a.out_nb_h;
         *reinterpret_cast<float4*>(orow + c) = v;
         return;
@@ -114,8 +134,9 @@ __device__ __forceinline__ void store_out4(const AttnArgs& a, int kvh, int r, in
 
 // After all of a kv head's rows were stored (by the threads that named barrier `bar_id` joins):
 // make them visible system-wide, then count the head on every rank.
+template <bool kPeer>
 __device__ __forceinline__ void signal_peers(const AttnArgs& a, int bar_id, int n_threads) {
-    if (a.n_peers == 0) return;
+    if (!kPeer) return;
     __threadfence_system();
     __syncwarp();
     asm volatile("barrier.sync %0, %1;" ::"r"(bar_id), "r"(n_threads) : "memory");
@@ -135,11 +156,11 @@ __device__ __forceinline__ void wait_gather(const AttnArgs& a) {
     }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kThreads, 2)
+template <int HD, int KVT, bool kPeer>
+__global__ void __launch_bounds__(kThreads, GqaCfg<HD, KVT>::MIN_BLOCKS)
 fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                      const __grid_constant__ AttnArgs a) {
-    using C = GqaCfg<HD>;
+    using C = GqaCfg<HD, KVT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
@@ -180,6 +201,9 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         // ============================ merger: sum the splits' partials of this kv head
         constexpr int G4m = HD / 4;
         const int gi = threadIdx.x, n_gm = R * G4m;
+        // the parameters the merge and the stores read, into the constant cache before the wait (a
+        // cold line read after it would sit on the launch's critical path)
+        asm volatile("" ::"l"(a.out), "l"(a.out_nb_t), "l"(a.out_nb_h), "r"(a.G), "r"(a.n_splits), "l"(a.err));
         pdl_wait();   // the output may still be in use by the previous launch
         if (threadIdx.x == 0) pdl_trigger();   // the splits decide when the next launch may start
         // every thread reaches the final signal (a named barrier when the gather is fused in)
@@ -208,9 +232,9 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 }
             }
             const float inv = LL > 0.0f ? 1.0f / LL : 0.0f;
-            store_out4(a, kvh, r, c, make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv));
+            store_out4<kPeer>(a, kvh, r, c, make_float4(o4.x * inv, o4.y * inv, o4.z * inv, o4.w * inv));
         }
-        signal_peers(a, 3, kThreads);
+        signal_peers<kPeer>(a, 3, kThreads);
         return;
     }
 
@@ -219,10 +243,15 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         uint8_t* kst = smem + s * C::STAGE_B;
         uint8_t* vst = kst + C::TILE_B;
         mbar_arrive_expect_tx(&full[s], 2 * C::TILE_B);
+        if constexpr (C::Q8) {     // q8_0 rows as 16-bit units, one unswizzled box per tensor
+            tma_load_2d(kst, &tmk, kvh * (C::HEADB / 2), y, &full[s]);
+            tma_load_2d(vst, &tmv, kvh * (C::HEADB / 2), y, &full[s]);
+        } else {
 #pragma unroll
-        for (int b = 0; b < C::NB; b++) {
-            tma_load_2d(kst + b * C::BOXB, &tmk, kvh * HD + b * C::COLS, y, &full[s]);
-            tma_load_2d(vst + b * C::BOXB, &tmv, kvh * HD + b * C::COLS, y, &full[s]);
+            for (int b = 0; b < C::NB; b++) {
+                tma_load_2d(kst + b * C::BOXB, &tmk, kvh * HD + b * C::COLS, y, &full[s]);
+                tma_load_2d(vst + b * C::BOXB, &tmv, kvh * HD + b * C::COLS, y, &full[s]);
+            }
         }
     };
 
@@ -258,14 +287,20 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
             // long context would evict itself before use)
             const int pf_end = min(nt_pf, C::STAGES + kL2Ahead);
             for (int j = j0; j < pf_end; j++) {
+                if constexpr (C::Q8) {
+                    tma_prefetch_l2_2d(&tmk, kvh * (C::HEADB / 2), a.row_base + ks0 + j * kBK);
+                    tma_prefetch_l2_2d(&tmv, kvh * (C::HEADB / 2), a.row_base + ks0 + j * kBK);
+                } else {
 #pragma unroll
-                for (int b = 0; b < C::NB; b++) {
-                    tma_prefetch_l2_2d(&tmk, kvh * HD + b * C::COLS, a.row_base + ks0 + j * kBK);
-                    tma_prefetch_l2_2d(&tmv, kvh * HD + b * C::COLS, a.row_base + ks0 + j * kBK);
+                    for (int b = 0; b < C::NB; b++) {
+                        tma_prefetch_l2_2d(&tmk, kvh * HD + b * C::COLS, a.row_base + ks0 + j * kBK);
+                        tma_prefetch_l2_2d(&tmv, kvh * HD + b * C::COLS, a.row_base + ks0 + j * kBK);
+                    }
                 }
             }
         }
     }
+    const bool do_gather_wait = kPeer && a.wait_ctr != nullptr;   // decided before the dependency wait
     if (warp < kCWarps) {
         // bring the launch's parameters into this SM's constant cache now: after the wait every
         // first touch of a cold parameter line would add a memory round trip to the critical path
@@ -274,12 +309,15 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         asm volatile("" ::"r"(a.n_new), "l"(a.knew), "l"(a.vnew), "l"(a.new_nb_t), "l"(a.kc_w), "l"(a.vc_w),
                      "l"(a.cache_row_bytes), "l"(a.err), "r"(a.cluster_merge), "r"(a.n_splits),
                      "l"(a.causal_base_dev), "r"(a.causal_base), "r"(a.row_base));
+        if (kPeer)
+            asm volatile("" ::"l"(a.peer_out), "l"(a.peer_ctr), "r"(a.head_offset), "l"(a.peer_nb_t),
+                         "l"(a.wait_ctr), "l"(a.epoch_dev), "r"(a.wait_per_epoch));
     }
     pdl_wait();
 
     // with the gather fused in, the query rows may depend on the previous layer's gathered output:
     // thread 0 waits (bounded) for its arrival count, then the consumer warps go on
-    if (a.wait_ctr && warp < kCWarps) {
+    if (do_gather_wait && warp < kCWarps) {
         if (threadIdx.x == 0) wait_gather(a);
         __syncwarp();
         asm volatile("barrier.sync 1, %0;" ::"n"(kCThreads) : "memory");
@@ -389,9 +427,9 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         uint8_t* kst = smem + s * C::STAGE_B;
         uint8_t* vst = kst + C::TILE_B;
         if (kw < ke) {
-            // fused append: a key this launch appends is written to the cache from its source row and
-            // patched into the tile the TMA brought in (which may hold the old row)
-            if (a.n_new > 0 && kw < cbase + a.n_new && kw + 16 > cbase) {
+            // fused append (f16 caches): a key this launch appends is written to the cache from its
+            // source row and patched into the tile the TMA brought in (which may hold the old row)
+            if (!C::Q8 && a.n_new > 0 && kw < cbase + a.n_new && kw + 16 > cbase) {
                 constexpr int LANES = HD * 2 / 16;
                 const int k_lo = max(kw, cbase), k_hi = min(kw + 16, cbase + a.n_new);
                 for (int key = k_lo; key < k_hi; key++) {
@@ -414,7 +452,7 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
             }
             // ---- S^T = K Q^T: four accumulator chains over the head-dim blocks
             float sacc[4][4] = {};
-            {
+            if constexpr (!C::Q8) {
                 const int krow = 16 * wig + (lane & 15);
                 const uint32_t kbase = smem_u32(kst);
 #pragma unroll
@@ -425,6 +463,48 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                             af[2], af[3]);
                     mma_f16(sacc[kk & 3], af, qb[kk][0], qb[kk][1]);
                 }
+            } else {
+                // q8_0: the A fragments straight from the raw rows (int8 pairs -> exact f16 integers);
+                // each 32-column block sums in a fresh accumulator scaled by its key's d, so K enters
+                // exactly as the oracle dequantises it
+                const uint8_t* kr0 = kst + (16 * wig + gq) * C::HEADB;     // key gq of this warp
+                const uint8_t* kr1 = kr0 + 8 * C::HEADB;                    // key gq + 8
+#pragma unroll
+                for (int b = 0; b < HD / kQK8_0; b++) {
+                    float sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        const int c0 = 2 + b * kQ8_0Bytes + h * 16 + 2 * tq;
+                        uint32_t af[4];
+                        af[0] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr0 + c0));
+                        af[1] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr1 + c0));
+                        af[2] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr0 + c0 + 8));
+                        af[3] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr1 + c0 + 8));
+                        mma_f16(sb, af, qb[2 * b + h][0], qb[2 * b + h][1]);
+                    }
+                    const float d0 = h2f(*reinterpret_cast<const uint16_t*>(kr0 + b * kQ8_0Bytes));
+                    const float d1 = h2f(*reinterpret_cast<const uint16_t*>(kr1 + b * kQ8_0Bytes));
+                    float* acc = sacc[b & 3];
+                    acc[0] = fmaf(d0, sb[0], acc[0]);
+                    acc[1] = fmaf(d0, sb[1], acc[1]);
+                    acc[2] = fmaf(d1, sb[2], acc[2]);
+                    acc[3] = fmaf(d1, sb[3], acc[3]);
+                }
+                // expand this warp's 16 V rows into f16 integers (128-byte swizzled [16][HD])
+                uint8_t* wst = smem + C::STG_OFF + warp * C::WST_B;
+                const uint8_t* vr = vst + (16 * wig) * C::HEADB;
+#pragma unroll 4
+                for (int task = lane; task < 16 * (HD / 8); task += 32) {
+                    const int kr = task / (HD / 8), e = (task % (HD / 8)) * 8;
+                    const uint8_t* src = vr + kr * C::HEADB + 2 + (e / kQK8_0) * kQ8_0Bytes + (e % kQK8_0);
+                    uint4 v;
+                    v.x = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src));
+                    v.y = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src + 2));
+                    v.z = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src + 4));
+                    v.w = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src + 6));
+                    *reinterpret_cast<uint4*>(wst + (e / C::COLS) * (16 * C::PITCH) + swz_off(kr, e % C::COLS, C::PITCH)) = v;
+                }
+                __syncwarp();
             }
             // ---- scale + mask (log2 domain); element i: key kw + gq + 8*(i>>1), column 2*tq + (i&1)
             float sv[4];
@@ -465,7 +545,7 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
             const uint32_t pb0 = movmatrix_t(pack_h2(p[0], p[1]));   // keys 0-7
             const uint32_t pb1 = movmatrix_t(pack_h2(p[2], p[3]));   // keys 8-15
             // ---- O^T += V^T P^T
-            {
+            if constexpr (!C::Q8) {
                 const int vrow = 16 * wig + (lane & 7) + 8 * (lane >> 4);
                 const uint32_t vbase = smem_u32(vst);
 #pragma unroll
@@ -475,6 +555,41 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                     ldsm_x4_t(vbase + (e / C::COLS) * C::BOXB + swz_off(vrow, e % C::COLS, C::PITCH), af[0], af[1],
                               af[2], af[3]);
                     mma_f16(o[n], af, pb0, pb1);
+                }
+            } else {
+                // q8_0: V as exact f16 integers from the warp's staging; each 32-column block's d is
+                // folded into P (keys 2tq, 2tq+1, 2tq+8, 2tq+9 of the B fragment), split into f16 hi +
+                // lo parts so P*d enters without a second rounding
+                const uint8_t* wst = smem + C::STG_OFF + warp * C::WST_B;
+                const uint8_t* vr = vst + (16 * wig) * C::HEADB;
+                const float2 pA = __half22float2(*reinterpret_cast<const __half2*>(&pb0));
+                const float2 pB = __half22float2(*reinterpret_cast<const __half2*>(&pb1));
+                const int vrow = (lane & 7) + 8 * (lane >> 4);
+                const uint32_t vbase = smem_u32(wst);
+#pragma unroll
+                for (int blk = 0; blk < HD / kQK8_0; blk++) {
+                    const float x[4] = {
+                        pA.x * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq) * C::HEADB + blk * kQ8_0Bytes)),
+                        pA.y * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq + 1) * C::HEADB + blk * kQ8_0Bytes)),
+                        pB.x * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq + 8) * C::HEADB + blk * kQ8_0Bytes)),
+                        pB.y * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq + 9) * C::HEADB + blk * kQ8_0Bytes))};
+                    float hi[4], lo[4];
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        hi[k] = __half2float(__float2half_rn(x[k]));
+                        lo[k] = x[k] - hi[k];
+                    }
+                    const uint32_t bh0 = pack_h2(hi[0], hi[1]), bh1 = pack_h2(hi[2], hi[3]);
+                    const uint32_t bl0 = pack_h2(lo[0], lo[1]), bl1 = pack_h2(lo[2], lo[3]);
+#pragma unroll
+                    for (int n = 2 * blk; n < 2 * blk + 2; n++) {
+                        const int e = n * 16 + 8 * ((lane >> 3) & 1);
+                        uint32_t af[4];
+                        ldsm_x4_t(vbase + (e / C::COLS) * (16 * C::PITCH) + swz_off(vrow, e % C::COLS, C::PITCH),
+                                  af[0], af[1], af[2], af[3]);
+                        mma_f16(o[n], af, bh0, bh1);
+                        mma_f16(o[n], af, bl0, bl1);
+                    }
                 }
             }
         }
@@ -530,9 +645,9 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 acc.x += v.x * sc; acc.y += v.y * sc; acc.z += v.z * sc; acc.w += v.w * sc;
             }
             const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            store_out4(a, kvh, r, c, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+            store_out4<kPeer>(a, kvh, r, c, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
         }
-        signal_peers(a, 1, kCThreads);
+        signal_peers<kPeer>(a, 1, kCThreads);
         return;
     }
 
@@ -624,10 +739,10 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 const float4 v = part[sub * n_g + gi];
                 acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
             }
-            store_out4(a, kvh, r, c, acc);
+            store_out4<kPeer>(a, kvh, r, c, acc);
         }
         if (tid == 0) a.tickets[kvh] = 0;
-        signal_peers(a, 1, kCThreads);
+        signal_peers<kPeer>(a, 1, kCThreads);
         return;
     }
 
@@ -657,34 +772,35 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     if (c == 0) st_async_f2(dsmem_map(smem_u32(&slot_ml[(split * kRows + r) * 2]), 0), make_float2(M, L), bar);
 }
 
-template <int HD>
+template <int HD, int KVT, bool kPeer = false>
 cudaError_t prepare_gqa() {
     static cudaError_t status = [] {
-        cudaError_t e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             GqaCfg<HD>::SMEM + 1024);
+        cudaError_t e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, GqaCfg<HD, KVT>::SMEM + 1024);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer>,
+                                     cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         return e;
     }();
     return status;
 }
 
-template <int HD>
+template <int HD, int KVT, bool kPeer>
 cudaError_t launch_gqa_t(const AttnArgs& a, const CUtensorMap* tk, const CUtensorMap* tv, cudaStream_t st) {
-    cudaError_t e = prepare_gqa<HD>();
+    cudaError_t e = prepare_gqa<HD, KVT, kPeer>();
     if (e != cudaSuccess) return e;
     // a cluster merge adds one merger CTA per kv head (cluster = splits + 1)
     const int nx = a.cluster_merge ? a.n_splits + 1 : a.n_splits;
     dim3 grid((unsigned)nx, (unsigned)a.NKV, 1u);
-    return launch_pdl_cluster(fa_decode_gqa_kernel<HD>, grid, dim3(kThreads), (size_t)GqaCfg<HD>::SMEM + 1024, st,
+    return launch_pdl_cluster(fa_decode_gqa_kernel<HD, KVT, kPeer>, grid, dim3(kThreads), (size_t)GqaCfg<HD, KVT>::SMEM + 1024, st,
                               a.cluster_merge ? nx : 1, *tk, *tv, a);
 }
 
-template <int HD>
+template <int HD, int KVT>
 int max_cluster_gqa() {
     static int v = -1;
     if (v < 0) {
-        if (prepare_gqa<HD>() != cudaSuccess) {
+        if (prepare_gqa<HD, KVT>() != cudaSuccess) {
             cudaGetLastError();
             v = 1;
             return v;
@@ -692,9 +808,9 @@ int max_cluster_gqa() {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(16, 1, 1);
         cfg.blockDim = dim3(kThreads);
-        cfg.dynamicSmemBytes = GqaCfg<HD>::SMEM + 1024;
+        cfg.dynamicSmemBytes = GqaCfg<HD, KVT>::SMEM + 1024;
         int n = 0;
-        if (cudaOccupancyMaxPotentialClusterSize(&n, fa_decode_gqa_kernel<HD>, &cfg) != cudaSuccess) {
+        if (cudaOccupancyMaxPotentialClusterSize(&n, fa_decode_gqa_kernel<HD, KVT, false>, &cfg) != cudaSuccess) {
             cudaGetLastError();
             n = 1;
         }
@@ -706,22 +822,33 @@ int max_cluster_gqa() {
 }  // namespace
 
 bool decode_gqa_applies(int head_dim, int kv_type, int T, int G, int mask_mode) {
-    if (kv_type != SV_TYPE_F16 || (head_dim != 64 && head_dim != 128)) return false;
     if (mask_mode != SV_MASK_CAUSAL && mask_mode != SV_MASK_NONE) return false;
-    return T * G <= kRows;
+    if (kv_type == SV_TYPE_F16 && (head_dim == 64 || head_dim == 128)) return T * G <= kRows;
+    if (kv_type == SV_TYPE_Q8_0 && head_dim == 256) return T * G <= GqaCfg<256, SV_TYPE_Q8_0>::ROWS_MAX;
+    return false;
 }
 
-int decode_gqa_max_cluster(int head_dim) {
-    return head_dim == 128 ? max_cluster_gqa<128>() : head_dim == 64 ? max_cluster_gqa<64>() : 1;
+int decode_gqa_ctas_per_sm(int kv_type) { return kv_type == SV_TYPE_Q8_0 ? 1 : 2; }
+
+int decode_gqa_max_cluster(int head_dim, int kv_type) {
+    if (kv_type == SV_TYPE_Q8_0) return head_dim == 256 ? max_cluster_gqa<256, SV_TYPE_Q8_0>() : 1;
+    return head_dim == 128 ? max_cluster_gqa<128, SV_TYPE_F16>()
+                           : head_dim == 64 ? max_cluster_gqa<64, SV_TYPE_F16>() : 1;
 }
 
-cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
-                              cudaStream_t st) {
+cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, int kv_type, const CUtensorMap* tk,
+                              const CUtensorMap* tv, cudaStream_t st) {
     if (a.n_qtiles != 1 || a.T * a.G > kRows || (a.n_splits > 1 && !a.cluster_merge && !a.tickets))
         return cudaErrorInvalidValue;
+    // the fused gather is a separate instantiation, so the plain decode carries none of its code
+    if (kv_type == SV_TYPE_Q8_0)
+        return head_dim == 256 ? launch_gqa_t<256, SV_TYPE_Q8_0, false>(a, tk, tv, st) : cudaErrorInvalidValue;
+    const bool peer = a.n_peers > 0;
     switch (head_dim) {
-        case 64: return launch_gqa_t<64>(a, tk, tv, st);
-        case 128: return launch_gqa_t<128>(a, tk, tv, st);
+        case 64: return peer ? launch_gqa_t<64, SV_TYPE_F16, true>(a, tk, tv, st)
+                             : launch_gqa_t<64, SV_TYPE_F16, false>(a, tk, tv, st);
+        case 128: return peer ? launch_gqa_t<128, SV_TYPE_F16, true>(a, tk, tv, st)
+                              : launch_gqa_t<128, SV_TYPE_F16, false>(a, tk, tv, st);
         default: return cudaErrorInvalidValue;
     }
 }

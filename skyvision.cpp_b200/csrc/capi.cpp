@@ -374,7 +374,7 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     // split-K merged inside a thread-block cluster (DSMEM) when the splits fit in one cluster
     // (the GQA kernel's cluster holds the splits plus one merger CTA)
     const int cmax = (allow_cluster && !window && clusters_enabled())
-                         ? (gqa ? decode_gqa_max_cluster(head_dim) - 1 : decode_max_cluster(head_dim, kv_type))
+                         ? (gqa ? decode_gqa_max_cluster(head_dim, kv_type) - 1 : decode_max_cluster(head_dim, kv_type))
                          : 1;
     Plan p;
     bool use_cluster = false;
@@ -389,8 +389,9 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     } else {
         // per-query windows differ in length (multi-session batches): aim for several waves of
         // CTAs so the short sessions' idle splits do not leave SMs waiting on the long ones
-        // (the GQA kernel runs two CTAs per SM)
-        const int target = window ? 8 * target_ctas_default() : (gqa ? 2 : 1) * target_ctas_default();
+        // (the f16 GQA kernel runs two CTAs per SM)
+        const int target = window ? 8 * target_ctas_default()
+                                  : (gqa ? decode_gqa_ctas_per_sm(kv_type) : 1) * target_ctas_default();
         p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0, target);
         a.cluster_merge = 0;
     }
@@ -404,7 +405,7 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
         a.ws_ml = ws + n_part * head_dim;
         a.tickets = tickets;
     }
-    if (gqa && a.n_qtiles == 1) return cuda_status(launch_decode_gqa(a, head_dim, tk, tv, st));
+    if (gqa && a.n_qtiles == 1) return cuda_status(launch_decode_gqa(a, head_dim, kv_type, tk, tv, st));
     return cuda_status(launch_decode(a, head_dim, kv_type, tk, tv, st));
 }
 
@@ -655,6 +656,7 @@ int sv_attn_append_at_peer(sv_kv* kv, int layer, const void* q, int q_type, cons
         wait_slot >= peer->n_slots || head_offset < 0 || head_offset + n_head > n_head_total)
         return SV_ERR_INVALID;
     if (peer->device != kv->device) return SV_ERR_INVALID;
+    if (kv->type != SV_TYPE_F16) return SV_ERR_UNSUPPORTED;   // the append is fused for f16 caches only
     if (n_head % kv->n_kv_head != 0) return SV_ERR_UNSUPPORTED;
     const int G = n_head / kv->n_kv_head;
     const int HD = kv->head_dim;

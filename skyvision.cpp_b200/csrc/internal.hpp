@@ -124,11 +124,13 @@ bool make_decode_tmap(CUtensorMap* m, const void* base, int kv_type, int head_di
                       size_t row_bytes, int64_t n_rows);
 size_t decode_partial_floats(int head_dim);   // floats per (tile, split) partial incl. m/l
 int decode_max_cluster(int head_dim, int kv_type);   // largest co-schedulable cluster (<= 16), 1 = none
-// GQA decode kernel (attn_decode_gqa.cu): f16 cache, HD 64/128, causal or no mask, T*G <= 8 rows
+// GQA decode kernel (attn_decode_gqa.cu): f16 cache HD 64/128 (T*G <= 8 rows) or q8_0 cache HD 256
+// (T*G <= 4), causal or no mask
 bool decode_gqa_applies(int head_dim, int kv_type, int T, int G, int mask_mode);
-int decode_gqa_max_cluster(int head_dim);
-cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv,
-                              cudaStream_t st);
+int decode_gqa_max_cluster(int head_dim, int kv_type);
+int decode_gqa_ctas_per_sm(int kv_type);
+cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, int kv_type, const CUtensorMap* tk,
+                              const CUtensorMap* tv, cudaStream_t st);
 int decode_block_keys();                       // BK
 cudaError_t launch_decode(const AttnArgs& a, int head_dim, int kv_type, const CUtensorMap* tk,
                           const CUtensorMap* tv, cudaStream_t st);
