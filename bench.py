@@ -747,7 +747,8 @@ def run_cfg4(sv, dev, stream):
                     "512-token chunks, 256 decode steps",
         "prefill_tflops": pre_flop / (pre_ms * 1e-3) / 1e12,
         "prefill_ms": pre_ms,
-        "prefill_kernel": "split-K mma.sync kernel with exact q8_0 folding (the tcgen05 kernel serves f16 caches)",
+        "prefill_kernel": "per chunk and layer: q8_0_split_kernel (visible rows -> f16 hi + lo planes), then "
+                          "fa_prefill_kernel<256, 1, 2> (tcgen05/TMEM, both parts of K and V through the MMA)",
         "decode_tokens_per_s": DEC4 / (dec_ms * 1e-3),
         "decode_kv_gbs": dec_bytes / (dec_ms * 1e-3) / 1e9,
     }
@@ -762,8 +763,8 @@ def check_flags(kv, stream=None):
 def run_kernels(args):
     """Each kernel of the path on a small single-layer case, 3 launches each in this order:
     fused decode (config 2 geometry, S = 4481), windowed decode (2 sessions of ~19k rows),
-    chunked prefill (384 over 4096), f16 and q8_0 append, compaction, q8_0 decode (config 4
-    geometry).  Under 1 GB on the device; used by the committed ncu summaries."""
+    chunked prefill (384 over 4096), f16 and q8_0 append, compaction, q8_0 decode and the last q8_0
+    prefill chunk (config 4 geometry: q8_0_split_kernel, then the tensor-core kernel on hi + lo parts).  Under 1 GB on the device; used by the committed ncu summaries."""
     import torch
     from __graft_entry__ import load_package
     sv = load_package()
@@ -816,6 +817,8 @@ def run_kernels(args):
     npq = torch.full((1,), 8192, dtype=torch.int32, device=dev)
     q4 = torch.randn(1, 16, 256, generator=g, device=dev).half()
     timed("decode_q8_0_us", lambda: kq.attn_at(0, q4, npq, 8193, 1 / 16.0))
+    q5 = torch.randn(512, 16, 256, generator=g, device=dev).half()
+    timed("prefill_q8_0_us", lambda: kq.attn(0, q5, n_past=8192 - 512, scale=1 / 16.0))
     torch.cuda.synchronize()
     assert kv.error_flags() == 0 and kq.error_flags() == 0 and kw.error_flags() == 0
     print(json.dumps({"workload": "kernels", "us_per_launch": times}), flush=True)

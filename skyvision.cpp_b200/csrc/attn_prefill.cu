@@ -13,9 +13,9 @@
 //   softmax warps (4 per query tile; warp w reads TMEM lane quarter w % 4, one row per thread):
 //              per 64-key tile read S (64 columns) with tcgen05.ld, apply scale and the causal
 //              predicate, take the row max, write P = exp2(S - m) as f16 over the first 32
-//              columns of the same TMEM buffer (the P.V MMA reads A from TMEM), and, only when
-//              the row max grew by more than 2^8, rescale the row of O in TMEM (exact: the final
-//              O / l uses the same stale max).  One exponential in four runs on the FMA pipe
+//              columns of the same TMEM buffer (the P.V MMA reads A from TMEM), and, when the
+//              row max grew, rescale the row of O in TMEM after the exponentials (which overlap
+//              the previous tile's P.V).  One exponential in four runs on the FMA pipe
 //              (exp2_fma) to take load off the SFU.
 //   TMA warp   lane 0 loads the query tiles (a 3D map over [T][NH][HD] whose {64, G, 128/G} box
 //              is one slab of a tile) and streams K tiles, lane 1 V tiles, each into its own ring
@@ -52,7 +52,12 @@ namespace svkv {
 
 namespace {
 
-constexpr float kRescaleLog2 = 8.0f;     // rescale O only when the max grows by > 2^8
+// O is rescaled whenever a row's max grows, so the largest weight of every tile is exactly 1 in f16.
+// (A lazy rescale that lets the running max trail by up to 2^8 saves the O round trips but rounds the
+// dominant weights: with x8 outlier V rows it cost ~1e-3 of max-abs error, measured on the GPU.)
+constexpr float kRescaleLog2 = 0.0f;
+// P parts on f16 caches (1: P rounded to f16, standard flash-attention precision)
+constexpr int kF16PParts = 1;
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
     uint64_t d = 0;
@@ -113,39 +118,45 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 
 // 2^x on the FMA pipe, for part of the softmax exponentials (the SFU's ex2 rate, 16 per clock per
 // SM, is below the tensor pipe's rate for 64-key tiles).  x = n + f with n = round(x), f in
-// [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here for minimax relative error on that interval
-// (iteratively reweighted least squares; max relative error 7.5e-5 in f32, under the f16 rounding
-// P gets anyway), and 2^n added into the exponent field.  x is clamped at -126 (2^-126 rounds to 0
-// in f16), and x <= 128 holds because P is taken against a running max that trails the true max
-// by at most 2^8.
+// [-0.5, 0.5]; 2^f by a degree-4 polynomial fitted here for minimax relative error on that interval
+// (Lawson's iteratively reweighted least squares; max relative error 2.7e-6 in f32 Horner form,
+// far under the f16 rounding P gets), and 2^n added into the exponent field.  A degree-3 fit
+// (7.5e-5) showed in the outputs of V rows with x8 outliers.  x is clamped at -126 (2^-126 rounds
+// to 0 in f16); x <= kRescaleLog2 because P is taken against the running max.
 __device__ __forceinline__ float exp2_fma(float x) {
     x = fmaxf(x, -126.0f);
     const float t = x + 12582912.0f;             // 1.5 * 2^23: round(x) lands in the low mantissa bits
     const float f = x - (t - 12582912.0f);
-    const float p = fmaf(fmaf(fmaf(0.05517166853f, f, 0.24261114001f), f, 0.69326096773f), f, 0.99992805719f);
+    const float p = fmaf(fmaf(fmaf(fmaf(0.00956530869f, f, 0.05591748655f), f, 0.2402486354f), f, 0.6931219101f), f,
+                         0.9999992251f);
     return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// NQT query tiles of 128 rows per CTA share every K/V tile (NQT = 2 at HD 128).
-template <int HD, int NQT>
+// NQT query tiles of 128 rows per CTA share every K/V tile (NQT = 2 at HD 128).  NP = 1: f16 cache
+// tiles; NP = 2: every K and V tile arrives as two f16 parts (hi, lo) whose sum is the exact
+// dequantised q8_0 value, and both parts go through the tensor core into the same accumulator.
+// The K and V rings hold single parts ("entries"), so a tile takes NP consecutive entries.
+template <int HD, int NQT, int NP = 1>
 struct PreCfg {
     static constexpr int BN = 64;                         // keys per tile
     static constexpr int BOX_ROW = 128;                   // bytes per swizzled row (64 f16)
     static constexpr int QBOX = 128 * BOX_ROW;            // one 64-column slab of a Q tile
     static constexpr int Q_B = (HD / 64) * QBOX;          // one Q tile
     static constexpr int KBOX = BN * BOX_ROW;             // one 64-column slab of a K or V tile
-    static constexpr int KV_B = (HD / 64) * KBOX;         // K (or V) bytes per stage
-    static constexpr int STAGE_B = 2 * KV_B;
-    static constexpr int NS_FIT = (227 * 1024 - NQT * Q_B - 2048) / STAGE_B;
-    static constexpr int NS = NS_FIT > 5 ? 5 : NS_FIT;    // K/V stages
-    static_assert(NS >= 2, "K/V ring needs two stages");
+    static constexpr int KV_B = (HD / 64) * KBOX;         // one part of a K (or V) tile: a ring entry
+    static constexpr int ENT_FIT = (227 * 1024 - NQT * Q_B - 2048) / KV_B;
+    // f16: up to 5 stages of (K, V); hi + lo parts: the entries that fit, split between K and V
+    static constexpr int NEK = NP == 1 ? (ENT_FIT / 2 > 5 ? 5 : ENT_FIT / 2) : ((ENT_FIT + 1) / 2 > 5 * NP ? 5 * NP : (ENT_FIT + 1) / 2);
+    static constexpr int NEV = NP == 1 ? NEK : (ENT_FIT / 2 > 5 * NP ? 5 * NP : ENT_FIT / 2);
+    static_assert(NEK >= 2 && NEK >= NP && NEV >= NP && NEV >= 2, "K/V rings need two entries and a whole tile");
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_ST = OFF_Q + NQT * Q_B;
-    static constexpr int OFF_BAR = OFF_ST + NS * STAGE_B;
-    static constexpr int N_BAR = 4 * NS + 1 + NQT * 6;
+    static constexpr int OFF_K = OFF_Q + NQT * Q_B;
+    static constexpr int OFF_V = OFF_K + NEK * KV_B;
+    static constexpr int OFF_BAR = OFF_V + NEV * KV_B;
+    static constexpr int N_BAR = 2 * NEK + 2 * NEV + 1 + NQT * 6;
     static constexpr int SMEM = OFF_BAR + N_BAR * 8 + 16;
     static_assert(SMEM + 1024 <= 227 * 1024, "shared memory budget");
     static constexpr int QCOLS = 128 + HD;                // per Q tile: S/P buffers [0, 64) and [64, 128), O after
@@ -196,22 +207,26 @@ __device__ __forceinline__ void softmax_sync() {
     asm volatile("barrier.sync 2, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
 }
 
-template <int HD, int NQT>
-__global__ void __launch_bounds__(PreCfg<HD, NQT>::THREADS, 1)
+// tmk/tmv: the f16 cache tensors, or (NP = 2) the hi parts; tmk2/tmv2: the lo parts (NP = 2 only).
+// PL = 2: P goes to the tensor core as f16 hi + lo parts (O += P_hi V + P_lo V_hi), so the weights
+// keep ~22 bits; PL = 1: P rounded to f16.
+template <int HD, int NQT, int NP, int PL>
+__global__ void __launch_bounds__(PreCfg<HD, NQT, NP>::THREADS, 1)
 fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                  const __grid_constant__ CUtensorMap tmk2, const __grid_constant__ CUtensorMap tmv2,
                   const __grid_constant__ CUtensorMap tmq, const __grid_constant__ AttnArgs a) {
-    using C = PreCfg<HD, NQT>;
+    using C = PreCfg<HD, NQT, NP>;
     constexpr int kSoftmaxWarps = C::SM_WARPS;
     constexpr int kTmaWarp = kSoftmaxWarps;   // then one MMA-issuer warp
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
     // K and V rings are separate so a K stage is refilled as soon as its S = Q K^T has completed
-    uint64_t* full_k = bars;              // [NS]
-    uint64_t* empty_k = bars + C::NS;     // [NS]
-    uint64_t* full_v = bars + 2 * C::NS;  // [NS]
-    uint64_t* empty_v = bars + 3 * C::NS; // [NS]
-    uint64_t* q_full = bars + 4 * C::NS;
+    uint64_t* full_k = bars;                          // [NEK]
+    uint64_t* empty_k = bars + C::NEK;                // [NEK]
+    uint64_t* full_v = bars + 2 * C::NEK;             // [NEV]
+    uint64_t* empty_v = bars + 2 * C::NEK + C::NEV;   // [NEV]
+    uint64_t* q_full = bars + 2 * C::NEK + 2 * C::NEV;
     uint64_t* s_full = q_full + 1;        // [NQT][2] per Q tile and S buffer
     // [NQT][2] P(i) written, by the parity of i: the softmax warps can finish tile i+1 before the
     // MMA warp has taken P(i) (S(i+1) is issued first), so one barrier would be two phases ahead
@@ -230,9 +245,11 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     const int nqt = (nq_all + QPT - 1) / QPT;            // Q tiles with any query (1..NQT)
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::NS; s++) {
+        for (int s = 0; s < C::NEK; s++) {
             mbar_init(&full_k[s], 1);
             mbar_init(&empty_k[s], 1);
+        }
+        for (int s = 0; s < C::NEV; s++) {
             mbar_init(&full_v[s], 1);
             mbar_init(&empty_v[s], 1);
         }
@@ -258,6 +275,10 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     if (warp == kTmaWarp && lane == 0) {
         tma_prefetch_desc(&tmk);
         tma_prefetch_desc(&tmv);
+        if (NP == 2) {
+            tma_prefetch_desc(&tmk2);
+            tma_prefetch_desc(&tmv2);
+        }
         if (a.q_tma) tma_prefetch_desc(&tmq);
     }
     tc_fence_before();
@@ -283,7 +304,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
         // Q tile qtl = warp / 4, TMEM lane quarter warp % 4 (rows 32*quarter + lane).  Per key tile:
         // S (64 columns) from TMEM, scale and causal mask, row max, P = exp2(S - m) written back as
         // f16 over the first 32 columns of the same TMEM buffer (the P.V MMA reads it from there),
-        // and, only when the row max grew by more than 2^8, O rescaled in TMEM.
+        // and, when the row max grew, O rescaled in TMEM.
         const int qtl = warp >> 2, quarter = warp & 3;
         const bool tile_live = qtl < nqt;
         const int r = quarter * 32 + lane;               // row = TMEM lane
@@ -359,8 +380,30 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                 m_use = mt;
                 resc = true;
             }
+            const float mneg = m_use == -INFINITY ? 0.0f : -m_use;
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[32];
+            uint32_t pl[PL == 2 ? 32 : 1];
+#pragma unroll
+            for (int k = 0; k < 64; k += 4) {
+                // three of every four on the SFU, one on the FMA pipe
+                const float p0 = fast_exp2(fmaf(s[k], c, mneg));
+                const float p1 = fast_exp2(fmaf(s[k + 1], c, mneg));
+                const float p2 = fast_exp2(fmaf(s[k + 2], c, mneg));
+                const float p3 = exp2_fma(fmaf(s[k + 3], c, mneg));
+                sum4[(k >> 2) & 3] += (p0 + p1) + (p2 + p3);
+                const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
+                pk[k >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
+                pk[(k >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+                if constexpr (PL == 2) {
+                    // p - f16(p) is exact in f32; its f16 rounding leaves ~2^-22 of p
+                    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                    pl[k >> 1] = pack_h2(p0 - f01.x, p1 - f01.y);
+                    pl[(k >> 1) + 1] = pack_h2(p2 - f23.x, p3 - f23.y);
+                }
+            }
+            // the exponentials above overlapped P.V(i-1); O is stable once it has completed
             if (__any_sync(0xffffffffu, resc)) {
-                // O is stable once P.V(i-1) has completed
                 if (!warp_wait(&od[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll 1
@@ -373,23 +416,10 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                     tmem_st32(lane_addr + 128 + cc, o);
                 }
             }
-            const float mneg = m_use == -INFINITY ? 0.0f : -m_use;
-            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t pk[32];
-#pragma unroll
-            for (int k = 0; k < 64; k += 4) {
-                // three of every four on the SFU, one on the FMA pipe
-                const float p0 = fast_exp2(fmaf(s[k], c, mneg));
-                const float p1 = fast_exp2(fmaf(s[k + 1], c, mneg));
-                const float p2 = fast_exp2(fmaf(s[k + 2], c, mneg));
-                const float p3 = exp2_fma(fmaf(s[k + 3], c, mneg));
-                sum4[(k >> 2) & 3] += (p0 + p1) + (p2 + p3);
-                pk[k >> 1] = pack_h2(p0, p1);
-                pk[(k >> 1) + 1] = pack_h2(p2, p3);
-            }
             // P over the first 32 columns of this tile's S buffer (S(i+2) reuses the buffer only
             // after P.V(i) has been issued, and the tensor pipe runs in order)
             tmem_st32(sbuf, reinterpret_cast<const float*>(pk));
+            if constexpr (PL == 2) tmem_st32(sbuf + 32, reinterpret_cast<const float*>(pl));   // P_lo after P_hi
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             tmem_wait_st();
             tc_fence_before();
@@ -550,23 +580,28 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                     tma_load_3d(smem + C::OFF_Q + q * C::Q_B + b * C::QBOX, &tmq, b * 64, kvh * a.G, t0 + q * QPT, q_full);
         }
         if (lane < 2 && n > 0) {
+            // ring entries in the order the MMA warp consumes them: tile i, part p -> entry i*NP + p
             const bool is_v = lane == 1;
             uint64_t* fullx = is_v ? full_v : full_k;
             uint64_t* emptyx = is_v ? empty_v : empty_k;
-            const CUtensorMap* tm = is_v ? &tmv : &tmk;
+            const int NE = is_v ? C::NEV : C::NEK;
+            uint8_t* ring = smem + (is_v ? C::OFF_V : C::OFF_K);
+            const int n_ent = n * NP;
             int issued = 0;
-            for (int i = 0; i < n; i++) {
-                const int s = i % C::NS;
-                if (i >= C::NS && !wait_or_abort(&emptyx[s], ((i / C::NS) - 1) & 1, a.err, abort_flag)) break;
-                uint8_t* dst = smem + C::OFF_ST + s * C::STAGE_B + (is_v ? C::KV_B : 0);
+            for (int e = 0; e < n_ent; e++) {
+                const int s = e % NE;
+                if (e >= NE && !wait_or_abort(&emptyx[s], ((e / NE) - 1) & 1, a.err, abort_flag)) break;
+                const int p = NP == 1 ? 0 : e % NP;
+                const CUtensorMap* tm = is_v ? (p ? &tmv2 : &tmv) : (p ? &tmk2 : &tmk);
+                uint8_t* dst = ring + s * C::KV_B;
                 mbar_arrive_expect_tx(&fullx[s], C::KV_B);
-                const int y = a.row_base + tile_of(i) * C::BN;
+                const int y = a.row_base + tile_of(e / NP) * C::BN;
 #pragma unroll
                 for (int b = 0; b < HD / 64; b++) tma_load_2d(dst + b * C::KBOX, tm, kvh * HD + b * 64, y, &fullx[s]);
-                issued = i + 1;
+                issued = e + 1;
             }
-            for (int i = max(0, issued - C::NS); i < issued; i++)
-                mbar_wait(&fullx[i % C::NS], (i / C::NS) & 1, a.err);
+            for (int e = max(0, issued - NE); e < issued; e++)
+                mbar_wait(&fullx[e % NE], (e / NE) & 1, a.err);
         }
         // never leave the Q copy in flight either (a CTA without keys does not wait for it otherwise)
         if (lane == 0 && a.q_tma) mbar_wait(q_full, 0, a.err);
@@ -576,46 +611,61 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
             const uint32_t idesc_s = umma_idesc(128, C::BN, 0, 0);
             const uint32_t idesc_o = umma_idesc(128, HD, 0, 1);
             const uint32_t q_base = smem_u32(smem + C::OFF_Q);
-            auto issue_s = [&](int i) {          // S(i) = Q K(i)^T into buffer i & 1 of every live Q tile
-                const uint32_t k_base = smem_u32(smem + C::OFF_ST + (i % C::NS) * C::STAGE_B);
+            // S(i) = Q K(i)^T into buffer i & 1 of every live Q tile, summed over the NP parts of K(i)
+            auto issue_s = [&](int i) -> bool {
+                for (int p = 0; p < NP; p++) {
+                    const int e = i * NP + p;
+                    if (!wait_or_abort(&full_k[e % C::NEK], (e / C::NEK) & 1, a.err, abort_flag)) return false;
+                }
+                tc_fence_after();
                 for (int q = 0; q < nqt; q++) {
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; kk++) {
-                        const uint64_t ad = umma_desc(q_base + q * C::Q_B + (kk / 4) * C::QBOX + (kk % 4) * 32, 16, 1024);
-                        const uint64_t bd = umma_desc(k_base + (kk / 4) * C::KBOX + (kk % 4) * 32, 16, 1024);
-                        umma_f16(tmem + q * C::QCOLS + (i & 1) * C::BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+                    for (int p = 0; p < NP; p++) {
+                        const uint32_t k_base = smem_u32(smem + C::OFF_K + ((i * NP + p) % C::NEK) * C::KV_B);
+#pragma unroll
+                        for (int kk = 0; kk < HD / 16; kk++) {
+                            const uint64_t ad = umma_desc(q_base + q * C::Q_B + (kk / 4) * C::QBOX + (kk % 4) * 32, 16, 1024);
+                            const uint64_t bd = umma_desc(k_base + (kk / 4) * C::KBOX + (kk % 4) * 32, 16, 1024);
+                            umma_f16(tmem + q * C::QCOLS + (i & 1) * C::BN, ad, bd, idesc_s, (kk > 0 || p > 0) ? 1u : 0u);
+                        }
                     }
                     umma_commit(&s_full[2 * q + (i & 1)]);
                 }
-                umma_commit(&empty_k[i % C::NS]);   // the K stage is free once every S(i) has completed
+                // the K entries are free once every S(i) has completed
+                for (int p = 0; p < NP; p++) umma_commit(&empty_k[(i * NP + p) % C::NEK]);
+                return true;
             };
             bool ok = wait_or_abort(q_full, 0, a.err, abort_flag);
-            if (ok) ok = wait_or_abort(&full_k[0], 0, a.err, abort_flag);
-            tc_fence_after();
-            if (ok) issue_s(0);
+            if (ok) ok = issue_s(0);
             for (int i = 0; ok && i < n; i++) {
                 // S(i+1) overlaps the softmax of tile i (its buffer held S(i-1), whose P.V was issued)
-                if (i + 1 < n) {
-                    const int s1 = (i + 1) % C::NS;
-                    if (!wait_or_abort(&full_k[s1], ((i + 1) / C::NS) & 1, a.err, abort_flag)) break;
-                    tc_fence_after();
-                    issue_s(i + 1);
+                if (i + 1 < n && !issue_s(i + 1)) break;
+                for (int p = 0; p < NP && ok; p++) {
+                    const int e = i * NP + p;
+                    ok = wait_or_abort(&full_v[e % C::NEV], (e / C::NEV) & 1, a.err, abort_flag);
                 }
-                if (!wait_or_abort(&full_v[i % C::NS], (i / C::NS) & 1, a.err, abort_flag)) break;
-                const uint32_t v_base = smem_u32(smem + C::OFF_ST + (i % C::NS) * C::STAGE_B) + C::KV_B;
                 for (int q = 0; q < nqt && ok; q++) {
                     if (!wait_or_abort(&p_full[2 * q + (i & 1)], (i >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t p_tmem = tmem + q * C::QCOLS + (i & 1) * C::BN;   // f16 P: 8 columns per 16 keys
+                    // f16 P: 8 columns per 16 keys; P_lo (PL = 2) in the next 32 columns
+                    const uint32_t p_tmem = tmem + q * C::QCOLS + (i & 1) * C::BN;
 #pragma unroll
-                    for (int kk = 0; kk < C::BN / 16; kk++) {
-                        const uint64_t bd = umma_desc(v_base + kk * 16 * 128, C::KBOX, 1024);
-                        umma_f16_ts(tmem + q * C::QCOLS + 128, p_tmem + kk * 8, bd, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+                    for (int p = 0; p < NP; p++) {
+                        const uint32_t v_base = smem_u32(smem + C::OFF_V + ((i * NP + p) % C::NEV) * C::KV_B);
+#pragma unroll
+                        for (int pp = 0; pp < (p == 0 ? PL : 1); pp++) {   // P_lo meets V's first part only
+#pragma unroll
+                            for (int kk = 0; kk < C::BN / 16; kk++) {
+                                const uint64_t bd = umma_desc(v_base + kk * 16 * 128, C::KBOX, 1024);
+                                umma_f16_ts(tmem + q * C::QCOLS + 128, p_tmem + pp * 32 + kk * 8, bd, idesc_o,
+                                            (i > 0 || p > 0 || pp > 0 || kk > 0) ? 1u : 0u);
+                            }
+                        }
                     }
                     umma_commit(&o_done[2 * q + (i & 1)]);
                 }
                 if (!ok) break;
-                umma_commit(&empty_v[i % C::NS]);
+                for (int p = 0; p < NP; p++) umma_commit(&empty_v[(i * NP + p) % C::NEV]);
             }
         }
     }
@@ -628,14 +678,15 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     }
 }
 
-template <int HD, int NQT>
+template <int HD, int NQT, int NP, int PL>
 cudaError_t prepare_t() {
     static cudaError_t status = [] {
-        using C = PreCfg<HD, NQT>;
-        cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             C::SMEM + 1024);
+        using C = PreCfg<HD, NQT, NP>;
+        cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM + 1024);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                                     1);
         return e;
     }();
     return status;
@@ -659,11 +710,11 @@ int pick_splits(int units, int tiles, size_t per_split_floats, size_t ws_floats,
     return best;
 }
 
-template <int HD, int NQT>
-cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensorMap* tv, float* ws,
-                     size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st) {
-    using C = PreCfg<HD, NQT>;
-    cudaError_t e = prepare_t<HD, NQT>();
+template <int HD, int NQT, int NP, int PL = NP>
+cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensorMap* tv, const CUtensorMap* tk2,
+                     const CUtensorMap* tv2, float* ws, size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st) {
+    using C = PreCfg<HD, NQT, NP>;
+    cudaError_t e = prepare_t<HD, NQT, NP, PL>();
     if (e != cudaSuccess) return e;
     AttnArgs a = a_in;
     const int QPT = 128 / a.G;
@@ -691,15 +742,51 @@ cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensor
                                  CU_TENSOR_MAP_SWIZZLE_128B) ? 1 : 0;
     }
     dim3 grid((unsigned)a.n_splits, (unsigned)n_cta_q, (unsigned)a.NKV);
-    return launch_pdl(fa_prefill_kernel<HD, NQT>, grid, dim3(C::THREADS), (size_t)(C::SMEM + 1024), st, *tk, *tv,
-                      tq, a);
+    return launch_pdl(fa_prefill_kernel<HD, NQT, NP, PL>, grid, dim3(C::THREADS), (size_t)(C::SMEM + 1024), st, *tk, *tv,
+                      NP == 2 ? *tk2 : *tk, NP == 2 ? *tv2 : *tv, tq, a);
+}
+
+// q8_0 rows -> f16 (hi, lo) parts for the tensor-core prefill.  x = q * d is exact in f32 (an 8-bit
+// integer times an 11-bit significand); hi = f16(x) and lo = f16(x - hi) (x - hi is exact in f32 and
+// has at most 8 significant bits), so hi + lo = x, the value the oracle's dequantisation gives, up
+// to f16 subnormal rounding of lo (< 2^-25).  One thread per 8 elements of one row of K or V;
+// planes[0..3] = K hi, K lo, V hi, V lo, each [row][ne0] f16.
+__global__ void __launch_bounds__(256) q8_0_split_kernel(const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
+                                                         size_t row_bytes, int ne0, int n_rows, uint16_t* planes,
+                                                         size_t plane_elems) {
+    pdl_wait();   // an earlier launch may still read the planes or write the rows
+    if (threadIdx.x == 0) pdl_trigger();
+    const int per_row = ne0 / 8;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)n_rows * per_row) return;
+    const int row = (int)(idx / per_row), e = (int)(idx % per_row) * 8;
+    const int is_v = blockIdx.y;
+    const uint8_t* blk = (is_v ? vc : kc) + (size_t)row * row_bytes + (size_t)(e / kQK8_0) * kQ8_0Bytes;
+    const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
+    const uint16_t* qs = reinterpret_cast<const uint16_t*>(blk + 2 + (e % kQK8_0));   // 2-byte aligned
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint16_t w = __ldg(qs + i);
+        const float x0 = (float)(int8_t)(w & 0xff) * d, x1 = (float)(int8_t)(w >> 8) * d;
+        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+        const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
+        hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+        lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+    }
+    uint16_t* dst = planes + (size_t)(2 * is_v) * plane_elems + (size_t)row * ne0 + e;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(dst + plane_elems) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 }  // namespace
 
 bool prefill_supported(int head_dim, int kv_type, int G, size_t row_bytes) {
-    return kv_type == SV_TYPE_F16 && (head_dim == 128 || head_dim == 256) && G >= 1 && G <= 16 && (128 % G) == 0 &&
-           row_bytes % 16 == 0;
+    if (!(G >= 1 && G <= 16 && (128 % G) == 0 && (head_dim == 128 || head_dim == 256))) return false;
+    if (kv_type == SV_TYPE_F16) return row_bytes % 16 == 0;
+    // q8_0 through the f16 (hi, lo) planes (rows of 16-byte multiples), at the head size the q8_0
+    // decode kernel serves
+    return kv_type == SV_TYPE_Q8_0 && head_dim == 256;
 }
 
 bool make_prefill_tmap(CUtensorMap* m, const void* base, int head_dim, int n_kv_head, size_t row_bytes,
@@ -709,13 +796,30 @@ bool make_prefill_tmap(CUtensorMap* m, const void* base, int head_dim, int n_kv_
 }
 
 cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv, float* ws,
-                           size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st) {
+                           size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st, const CUtensorMap* tk_lo,
+                           const CUtensorMap* tv_lo) {
+    // q8_0 (hi, lo parts of K and V): P as hi + lo too; f16 caches: P rounded to f16
+    const bool parts = tk_lo && tv_lo;
     // two query tiles per CTA when the chunk has them (each K/V tile then feeds 256 query rows)
-    if (head_dim == 128)
-        return a.T * a.G > 128 ? launch_t<128, 2>(a, tk, tv, ws, ws_floats, tickets, n_tickets, st)
-                               : launch_t<128, 1>(a, tk, tv, ws, ws_floats, tickets, n_tickets, st);
-    if (head_dim == 256) return launch_t<256, 1>(a, tk, tv, ws, ws_floats, tickets, n_tickets, st);
+    if (head_dim == 128) {
+        if (a.T * a.G > 128)
+            return parts ? launch_t<128, 2, 2>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st)
+                         : launch_t<128, 2, 1, kF16PParts>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st);
+        return parts ? launch_t<128, 1, 2>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st)
+                     : launch_t<128, 1, 1, kF16PParts>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st);
+    }
+    if (head_dim == 256)
+        return parts ? launch_t<256, 1, 2>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st)
+                     : launch_t<256, 1, 1, kF16PParts>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st);
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_q8_0_split(const uint8_t* kc, const uint8_t* vc, size_t row_bytes, int ne0, int n_rows,
+                              uint16_t* planes, size_t plane_elems, cudaStream_t st) {
+    if (n_rows <= 0) return cudaSuccess;
+    const int64_t threads = (int64_t)n_rows * (ne0 / 8);
+    dim3 grid((unsigned)((threads + 255) / 256), 2);
+    return launch_pdl(q8_0_split_kernel, grid, dim3(256), 0, st, kc, vc, row_bytes, ne0, n_rows, planes, plane_elems);
 }
 
 }  // namespace svkv

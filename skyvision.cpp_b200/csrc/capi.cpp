@@ -199,7 +199,24 @@ int sv_kv_create(int device, int n_layer, int n_kv_head, int head_dim, int n_ctx
                 return SV_ERR_CUDA;
             }
     }
-    if (prefill_supported(head_dim, kv_type, 4, kv->row_bytes)) {
+    if (kv_type == SV_TYPE_Q8_0 && prefill_supported(head_dim, kv_type, 4, kv->row_bytes)) {
+        // the tensor-core prefill reads a q8_0 layer as f16 (hi, lo) planes rebuilt per call
+        const size_t ne0 = (size_t)n_kv_head * head_dim;
+        const size_t xbytes = 4 * ne0 * (size_t)n_ctx * sizeof(uint16_t);
+        // zeroed once: rows past a call's keys stay finite (masked keys meet P = 0)
+        if (cudaMalloc(&kv->xbuf, xbytes) != cudaSuccess || cudaMemset(kv->xbuf, 0, xbytes) != cudaSuccess) {
+            cudaGetLastError();
+            sv_kv_destroy(kv);
+            return SV_ERR_NOMEM;
+        }
+        for (int i = 0; i < 4; i++)
+            if (!make_prefill_tmap(&kv->tm_x[i], kv->xbuf + (size_t)i * ne0 * n_ctx, head_dim, n_kv_head,
+                                   ne0 * sizeof(uint16_t), n_ctx)) {
+                sv_kv_destroy(kv);
+                return SV_ERR_CUDA;
+            }
+    }
+    if (kv_type == SV_TYPE_F16 && prefill_supported(head_dim, kv_type, 4, kv->row_bytes)) {
         kv->tm_pre.resize(2 * n_layer);
         for (int i = 0; i < 2 * n_layer; i++)
             if (!make_prefill_tmap(&kv->tm_pre[i], kv->tensor(i / 2, i % 2), head_dim, n_kv_head, kv->row_bytes,
@@ -221,6 +238,7 @@ int sv_kv_destroy(sv_kv* kv) {
     if (kv->tickets) cudaFree(kv->tickets);
     if (kv->err) cudaFree(kv->err);
     if (kv->scratch) cudaFree(kv->scratch);
+    if (kv->xbuf) cudaFree(kv->xbuf);
     delete kv;
     return SV_OK;
 }
@@ -355,10 +373,13 @@ static bool gqa_enabled() {
     return on;
 }
 
+// tkp/tvp: prefill-box maps of the f16 cache tensors, or of the hi planes of a q8_0 layer, whose lo
+// planes are then tkl/tvl
 static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* tv, const CUtensorMap* tkp,
                          const CUtensorMap* tvp, int head_dim, int kv_type, AttnArgs& a, int span, bool window,
                          float* ws, size_t ws_bytes, int* tickets, int n_tickets, cudaStream_t st,
-                         bool allow_cluster = false) {
+                         bool allow_cluster = false, const CUtensorMap* tkl = nullptr,
+                         const CUtensorMap* tvl = nullptr) {
     // A fused append + attention may fill its K/V ring before its grid dependency resolves only if
     // the launch before it on the stream did not write cache rows while letting it start early.
     a.ring_prefill = (kvh && !kvh->rows_written_last) ? 1 : 0;
@@ -366,7 +387,7 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
     // chunked prefill on the tensor-core kernel when it applies
     if (!window && tkp && tvp && a.mask_mode == SV_MASK_CAUSAL && a.T * a.G > 16) {
         return cuda_status(launch_prefill(a, head_dim, tkp, tvp, ws, ws ? ws_bytes / sizeof(float) : 0, tickets,
-                                          tickets ? n_tickets : 0, st));
+                                          tickets ? n_tickets : 0, st, tkl, tvl));
     }
     const size_t ws_floats = ws ? ws_bytes / sizeof(float) : 0;
     // grouped-query decode (one query tile of <= 8 rows per kv head) on the swap-AB kernel
@@ -440,9 +461,22 @@ int sv_attn(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, 
     a.err = kv->err;
     const CUtensorMap* tkp = kv->tm_pre.empty() ? nullptr : &kv->tm_pre[2 * layer];
     const CUtensorMap* tvp = kv->tm_pre.empty() ? nullptr : &kv->tm_pre[2 * layer + 1];
+    const CUtensorMap *tkl = nullptr, *tvl = nullptr;
+    if (kv->xbuf && T * a.G > 16 && prefill_supported(HD, kv->type, a.G, kv->row_bytes)) {
+        // q8_0 chunk: the keys it sees, rows [0, n_past + T), as f16 (hi, lo) planes, then the
+        // tensor-core kernel over the planes (each part through the MMA into the same accumulator)
+        const int ne0 = kv->n_kv_head * HD;
+        cudaError_t e = launch_q8_0_split(kv->tensor(layer, 0), kv->tensor(layer, 1), kv->row_bytes, ne0, n_past + T,
+                                          kv->xbuf, (size_t)ne0 * kv->n_ctx, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_status(e);
+        tkp = &kv->tm_x[0];
+        tkl = &kv->tm_x[1];
+        tvp = &kv->tm_x[2];
+        tvl = &kv->tm_x[3];
+    }
     return run_attention(kv, &kv->tm_dec[2 * layer], &kv->tm_dec[2 * layer + 1], tkp, tvp, HD, kv->type, a,
                          n_past + T, false, kv->ws, kv->ws_bytes, kv->tickets, kv->n_tickets,
-                         static_cast<cudaStream_t>(stream), /*allow_cluster=*/true);
+                         static_cast<cudaStream_t>(stream), /*allow_cluster=*/true, tkl, tvl);
 }
 
 int sv_attn_at(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_head, const int32_t* n_past_dev,

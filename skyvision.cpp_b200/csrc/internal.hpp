@@ -95,6 +95,10 @@ struct KvHandle {
     uint8_t* buf = nullptr;              // 2*n_layer tensors, K then V per layer
     std::vector<CUtensorMap> tm_dec;     // decode-box tensor maps: [2*layer + is_v]
     std::vector<CUtensorMap> tm_pre;     // prefill-box tensor maps (f16 caches), same indexing
+    // q8_0 caches: one layer's rows as f16 (hi, lo) planes for the tensor-core prefill (K hi, K lo,
+    // V hi, V lo; n_ctx rows each), rebuilt by every prefill call, and their prefill-box tensor maps
+    uint16_t* xbuf = nullptr;
+    CUtensorMap tm_x[4];
     float* ws = nullptr;                 // split-K partials
     size_t ws_bytes = 0;
     int* tickets = nullptr;
@@ -139,8 +143,15 @@ cudaError_t launch_decode(const AttnArgs& a, int head_dim, int kv_type, const CU
 bool prefill_supported(int head_dim, int kv_type, int G, size_t row_bytes);
 bool make_prefill_tmap(CUtensorMap* m, const void* base, int head_dim, int n_kv_head, size_t row_bytes,
                        int64_t n_rows);
+// tk_lo/tv_lo non-null: tk/tv map the hi parts and tk_lo/tv_lo the lo parts of a q8_0 cache's rows
+// (q8_0_split_kernel), and every K/V tile goes through the tensor core as hi + lo
 cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* tk, const CUtensorMap* tv, float* ws,
-                           size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st);
+                           size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st,
+                           const CUtensorMap* tk_lo = nullptr, const CUtensorMap* tv_lo = nullptr);
+// rows [0, n_rows) of one layer's q8_0 K and V tensors -> f16 planes K hi, K lo, V hi, V lo
+// (planes + i * plane_elems, each [row][ne0])
+cudaError_t launch_q8_0_split(const uint8_t* kc, const uint8_t* vc, size_t row_bytes, int ne0, int n_rows,
+                              uint16_t* planes, size_t plane_elems, cudaStream_t st);
 
 cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t dst_nb1,
                             const void* src, int src_type, size_t src_nb1, int64_t n_rows,

@@ -143,6 +143,21 @@ def test_prefill_chunks(orc, hd, nkv, nh, T, n_past):
     assert kv.error_flags() == 0
 
 
+@pytest.mark.parametrize("hd,nkv,nh,T,n_past", [(256, 4, 16, 512, 1024), (128, 8, 32, 384, 4096)])
+def test_prefill_chunks_f16_outliers(orc, hd, nkv, nh, T, n_past):
+    """f16 cache whose K/V carry 1% outliers x8 (config 4's distribution): the largest weights of
+    a peaked softmax must not pick up f16 rounding (the running max is kept current).  P itself is
+    rounded to f16 on f16 caches, so rows that see only a few keys (a prompt's first chunk) can
+    reach ~2.2e-3 on this distribution; those rows are covered on q8_0 caches, where P also
+    goes through the tensor core as hi + lo parts."""
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, nkv, hd, n_past + T + 64)
+    fill_cache(orc, kv, 0, n_past + T, seed=12, outliers=0.01)
+    q = orc.normal_f16(12, 2000 + T, T * nh * hd).reshape(T, nh, hd)
+    out = kv.attn(0, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / np.sqrt(hd))
+    close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n_past, 1 / np.sqrt(hd)))
+
+
 @pytest.mark.parametrize("hd,nkv,nh", [(64, 4, 16), (256, 4, 16), (128, 8, 8), (128, 2, 32), (32, 8, 8), (16, 2, 8)])
 def test_decode_head_geometries(orc, hd, nkv, nh):
     kv = sv.KvCache()
@@ -174,6 +189,47 @@ def test_decode_q8_0_outliers(orc, n_past, T):
     q = orc.normal_f16(3, 300 + n_past, T * 16 * 256).reshape(T, 16, 256)
     out = kv.attn(0, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / 16.0)
     close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n_past, 1 / 16.0))
+
+
+@pytest.mark.parametrize("hd,nkv,nh,T,n_past", [
+    (256, 4, 16, 512, 1024),     # a 512-token chunk over a q8_0 cache
+    (256, 4, 16, 512, 0),        # its first chunk
+    (256, 4, 16, 37, 2999),      # ragged chunk, one query tile, several key splits
+    (256, 4, 32, 100, 500),      # GQA 8:1 -> 16 queries per tile
+    (256, 8, 16, 130, 77),       # GQA 2:1, ragged second tile, short context
+])
+def test_prefill_chunks_q8_0(orc, hd, nkv, nh, T, n_past):
+    """Chunked prefill over a q8_0 cache (1% outliers x8): the tensor-core kernel on f16 (hi, lo) parts
+    of the exactly dequantised rows."""
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, nkv, hd, n_past + T + 64, sv.TYPE_Q8_0)
+    fill_cache(orc, kv, 0, n_past + T, seed=12, outliers=0.01)
+    q = orc.normal_f16(12, 2000 + T, T * nh * hd).reshape(T, nh, hd)
+    out = kv.attn(0, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=n_past, scale=1 / np.sqrt(hd))
+    close(out.cpu().numpy(), ref_attn(orc, kv, 0, q, n_past, 1 / np.sqrt(hd)))
+    assert kv.error_flags() == 0
+
+
+def test_prefill_q8_0_chunk_sequence(orc):
+    """Config 4's loop in small: per chunk, each of two layers quantises its rows into the cache and
+    attends; the (hi, lo) planes are shared by the layers and rebuilt by every call."""
+    NKV, HD, NH, CH, n_chunks = 4, 256, 16, 256, 3
+    kv = sv.KvCache()
+    assert kv.alloc(0, 2, NKV, HD, CH * n_chunks, sv.TYPE_Q8_0)
+    ne0 = NKV * HD
+    outs = []
+    for c in range(n_chunks):
+        for layer in range(2):
+            k = orc.normal_f16(13, 10 * c + layer, CH * ne0, outlier_frac=0.01).reshape(CH, ne0)
+            v = orc.normal_f16(13, 100 + 10 * c + layer, CH * ne0, outlier_frac=0.01).reshape(CH, ne0)
+            q = orc.normal_f16(13, 200 + 10 * c + layer, CH * NH * HD).reshape(CH, NH, HD)
+            kv.append(layer, torch.from_numpy(k.view(np.float16)).to(DEV),
+                      torch.from_numpy(v.view(np.float16)).to(DEV), base=c * CH)
+            out = kv.attn(layer, torch.from_numpy(q.view(np.float16)).to(DEV), n_past=c * CH, scale=1 / 16.0)
+            outs.append((layer, c, q, out.cpu().numpy()))
+    for layer, c, q, got in outs:
+        close(got, ref_attn(orc, kv, layer, q, c * CH, 1 / 16.0))
+    assert kv.error_flags() == 0
 
 
 # ------------------------------------------------------------------ explicit mask / ggml view form
