@@ -194,10 +194,12 @@ int sv_attn_at(sv_kv* kv, int layer, const void* q, int q_type, int T, int n_hea
  * append (ggml_set_rows of k_new/v_new at rows *n_past_dev + t,
  * qwen3vl_model.cpp:654-655) and the causal attention over the cache including
  * those rows (qwen3vl_model.cpp:657-663).  k_new/v_new: device f16
- * [T][n_kv_head*head_dim].  f16 caches with T*(n_head/n_kv_head) <= 16 run as
- * one kernel (the CTA that covers a new row writes it to the cache and uses it
- * from shared memory); other cases run sv_kv_append_at then sv_attn_at.
- * Graph-stable like sv_attn_at. */
+ * [T][n_kv_head*head_dim].  f16 caches with T*(n_head/n_kv_head) <= 16, and
+ * q8_0 caches at head_dim 256 with T*(n_head/n_kv_head) <= 4 (16-byte aligned
+ * sources), run as one kernel: the CTA that covers a new row writes it to the
+ * cache (q8_0: quantised with the same steps as sv_set_rows, bytes identical)
+ * and uses it from shared memory; other cases run sv_kv_append_at then
+ * sv_attn_at.  Graph-stable like sv_attn_at. */
 int sv_attn_append_at(sv_kv* kv, int layer, const void* q, int q_type, const void* k_new, const void* v_new, int T,
                       int n_head, const int32_t* n_past_dev, int max_keys, float scale, float* out, void* stream);
 

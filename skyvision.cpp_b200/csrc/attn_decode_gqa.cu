@@ -74,21 +74,65 @@ struct GqaCfg {
     static constexpr int PUSH_O = 0;
     static constexpr int PUSH_ML = 16 * kRows * HD * 4;
     static_assert(PUSH_ML + 16 * kRows * 8 <= RING_B, "merge slots must fit in the stage ring");
-    // q8_0: each consumer warp expands the V rows of its 16 keys into f16 integers here
-    static constexpr int WST_B = Q8 ? 16 * HD * 2 : 0;
-    static constexpr int STG_OFF = RING_B;
-    static constexpr int BAR_OFF = STG_OFF + kCWarps * WST_B;
+    static constexpr int BAR_OFF = RING_B;
     static constexpr int SMEM = BAR_OFF + (2 * STAGES + 1) * 8 + 16;   // + abort and last-split flags
     static_assert(SMEM + 1024 <= 227 * 1024, "shared memory budget");
 };
 
-// two signed bytes (low, high of w) -> exact f16x2 (1024 + (b + 128) - 1152)
-__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w) {
-    const uint32_t lo = (w & 0xffu) ^ 0x80u;
-    const uint32_t hi = ((w >> 8) & 0xffu) ^ 0x80u;
-    const uint32_t h = (0x6400u | lo) | ((0x6400u | hi) << 16);
+// Signed bytes -> exact f16 integers: with u = b ^ 0x80 = b + 128, the f16 bit pattern 0x64uu is
+// 1024 + u, and subtracting 1152 leaves b.  x = the four bytes of w after the XOR; sel picks two of
+// them into the low bytes of the two halves (byte_perm selector nibbles; 4 = the 0x64 byte).
+template <uint32_t kSel>
+__device__ __forceinline__ uint32_t u8x2_to_h2(uint32_t x) {
+    const uint32_t h = __byte_perm(x, 0x64646464u, kSel);
     __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __half2half2(__ushort_as_half(0x6480u)));
     return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// four bytes of a q8_0 row at p, which is 4-byte aligned when `aligned`, else 2-byte aligned (the
+// callers' loops are unrolled, so the branch folds away)
+__device__ __forceinline__ uint32_t ld_b4(const uint8_t* p, bool aligned) {
+    if (aligned) return *reinterpret_cast<const uint32_t*>(p);
+    return __byte_perm(*reinterpret_cast<const uint16_t*>(p), *reinterpret_cast<const uint16_t*>(p + 2), 0x5410);
+}
+
+// Fused q8_0 append: lane l quantises elements [8l, 8l + 8) of one kv head's source row (f16, 16-byte
+// aligned) with the steps of the append kernel (ggml's block_q8_0 rule: d = amax / 127, id = 1 / d,
+// q = round-half-away(x * id), d stored as f16), so the bytes match sv_set_rows exactly, and writes
+// them both to the cache row (gdst) and into the shared-memory tile that holds the row (sdst).  The
+// four lanes of a 32-element block are consecutive.  HD = 256: the warp covers the head.
+__device__ __forceinline__ void quantize_head_q8_0(const uint8_t* src, uint8_t* gdst, uint8_t* sdst, int lane) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + lane * 16);
+    const __half2* h = reinterpret_cast<const __half2*>(&u);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 f = __half22float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; k++) amax = fmaxf(amax, fabsf(v[k]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+    const int b = lane >> 2, sub = (lane & 3) * 8;
+    const int ob = b * kQ8_0Bytes;
+    if (sub == 0) {
+        const __half hd = __float2half_rn(dd);
+        *reinterpret_cast<__half*>(gdst + ob) = hd;   // 2-byte aligned (34 * b)
+        *reinterpret_cast<__half*>(sdst + ob) = hd;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+        const int q0 = (int)roundf(__fmul_rn(v[k], id));
+        const int q1 = (int)roundf(__fmul_rn(v[k + 1], id));
+        const uint16_t pr = (uint16_t)((uint8_t)(int8_t)q0 | ((uint16_t)(uint8_t)(int8_t)q1 << 8));
+        *reinterpret_cast<uint16_t*>(gdst + ob + 2 + sub + k) = pr;   // even offsets
+        *reinterpret_cast<uint16_t*>(sdst + ob + 2 + sub + k) = pr;
+    }
 }
 
 __device__ __forceinline__ void consumer_sync() {
@@ -338,7 +382,9 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         for (int kk = 0; kk < HD / 16; kk++) {
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-                const int e = kk * 16 + h * 8 + 2 * tq;
+                // q8_0: thread tq's fragment columns are the 4 consecutive elements at 4*tq of the
+                // k-step (in K and Q alike, so the dot products are unchanged)
+                const int e = C::Q8 ? kk * 16 + 4 * tq + 2 * h : kk * 16 + h * 8 + 2 * tq;
                 uint32_t v = 0;
                 if (valid) {
                     if (a.q_type == SV_TYPE_F32) {
@@ -450,6 +496,21 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 fence_proxy_async_smem();   // order these writes before the stage's next TMA fill
                 __syncwarp();
             }
+            // fused append (q8_0 caches): each appended key of this warp is quantised from its f16
+            // source row into the cache and into the tile the TMA brought in
+            if (C::Q8 && a.n_new > 0 && kw < cbase + a.n_new && kw + 16 > cbase) {
+                static_assert(!C::Q8 || HD == 256, "one warp quantises one kv head");
+                const int k_lo = max(kw, cbase), k_hi = min(kw + 16, cbase + a.n_new);
+                for (int key = k_lo; key < k_hi; key++) {
+                    const int row = key - (ks + j * kBK);
+                    const size_t so = (size_t)(key - cbase) * a.new_nb_t + (size_t)kvh * HD * 2;
+                    const size_t co = (size_t)key * a.cache_row_bytes + (size_t)kvh * C::HEADB;
+                    quantize_head_q8_0(a.knew + so, a.kc_w + co, kst + row * C::HEADB, lane);
+                    quantize_head_q8_0(a.vnew + so, a.vc_w + co, vst + row * C::HEADB, lane);
+                }
+                fence_proxy_async_smem();   // order these writes before the stage's next TMA fill
+                __syncwarp();
+            }
             // ---- S^T = K Q^T: four accumulator chains over the head-dim blocks
             float sacc[4][4] = {};
             if constexpr (!C::Q8) {
@@ -464,9 +525,11 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                     mma_f16(sacc[kk & 3], af, qb[kk][0], qb[kk][1]);
                 }
             } else {
-                // q8_0: the A fragments straight from the raw rows (int8 pairs -> exact f16 integers);
-                // each 32-column block sums in a fresh accumulator scaled by its key's d, so K enters
-                // exactly as the oracle dequantises it
+                // q8_0: the A fragments straight from the raw rows, 4 consecutive bytes per (key,
+                // k-step) and thread (a0 / a1 = its first pair, a2 / a3 its second); each 32-column
+                // block sums in a fresh accumulator scaled by its key's d, so K enters exactly as the
+                // oracle dequantises it.  A block's bytes start 2 + 34*b into the 4-byte aligned row:
+                // aligned for odd b, 2 bytes off for even b (both known at compile time).
                 const uint8_t* kr0 = kst + (16 * wig + gq) * C::HEADB;     // key gq of this warp
                 const uint8_t* kr1 = kr0 + 8 * C::HEADB;                    // key gq + 8
 #pragma unroll
@@ -474,12 +537,14 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                     float sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int h = 0; h < 2; h++) {
-                        const int c0 = 2 + b * kQ8_0Bytes + h * 16 + 2 * tq;
+                        const int c0 = 2 + b * kQ8_0Bytes + h * 16 + 4 * tq;
+                        const uint32_t x0 = ld_b4(kr0 + c0, (b & 1) == 1) ^ 0x80808080u;
+                        const uint32_t x1 = ld_b4(kr1 + c0, (b & 1) == 1) ^ 0x80808080u;
                         uint32_t af[4];
-                        af[0] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr0 + c0));
-                        af[1] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr1 + c0));
-                        af[2] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr0 + c0 + 8));
-                        af[3] = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(kr1 + c0 + 8));
+                        af[0] = u8x2_to_h2<0x4140>(x0);
+                        af[1] = u8x2_to_h2<0x4140>(x1);
+                        af[2] = u8x2_to_h2<0x4342>(x0);
+                        af[3] = u8x2_to_h2<0x4342>(x1);
                         mma_f16(sb, af, qb[2 * b + h][0], qb[2 * b + h][1]);
                     }
                     const float d0 = h2f(*reinterpret_cast<const uint16_t*>(kr0 + b * kQ8_0Bytes));
@@ -490,21 +555,6 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                     acc[2] = fmaf(d1, sb[2], acc[2]);
                     acc[3] = fmaf(d1, sb[3], acc[3]);
                 }
-                // expand this warp's 16 V rows into f16 integers (128-byte swizzled [16][HD])
-                uint8_t* wst = smem + C::STG_OFF + warp * C::WST_B;
-                const uint8_t* vr = vst + (16 * wig) * C::HEADB;
-#pragma unroll 4
-                for (int task = lane; task < 16 * (HD / 8); task += 32) {
-                    const int kr = task / (HD / 8), e = (task % (HD / 8)) * 8;
-                    const uint8_t* src = vr + kr * C::HEADB + 2 + (e / kQK8_0) * kQ8_0Bytes + (e % kQK8_0);
-                    uint4 v;
-                    v.x = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src));
-                    v.y = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src + 2));
-                    v.z = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src + 4));
-                    v.w = i8x2_to_h2(*reinterpret_cast<const uint16_t*>(src + 6));
-                    *reinterpret_cast<uint4*>(wst + (e / C::COLS) * (16 * C::PITCH) + swz_off(kr, e % C::COLS, C::PITCH)) = v;
-                }
-                __syncwarp();
             }
             // ---- scale + mask (log2 domain); element i: key kw + gq + 8*(i>>1), column 2*tq + (i&1)
             float sv[4];
@@ -557,22 +607,26 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                     mma_f16(o[n], af, pb0, pb1);
                 }
             } else {
-                // q8_0: V as exact f16 integers from the warp's staging; each 32-column block's d is
-                // folded into P (keys 2tq, 2tq+1, 2tq+8, 2tq+9 of the B fragment), split into f16 hi +
-                // lo parts so P*d enters without a second rounding
-                const uint8_t* wst = smem + C::STG_OFF + warp * C::WST_B;
+                // q8_0: the A fragments of V^T straight from the raw rows.  M-row gq of m-tile n is
+                // dim 16n + 2gq and M-row gq + 8 is dim 16n + 2gq + 1 (adjacent bytes of a key's row;
+                // the combine below puts the outputs back in order), keys in natural order: a0 / a1 =
+                // the two dims of keys 2tq, 2tq+1, a2 / a3 of keys 2tq+8, 2tq+9.  Each 32-column
+                // block's d is folded into P (keys 2tq, 2tq+1, 2tq+8, 2tq+9 of the B fragment), split
+                // into f16 hi + lo parts so P*d enters without a second rounding.
                 const uint8_t* vr = vst + (16 * wig) * C::HEADB;
+                const uint8_t* vk0 = vr + (2 * tq) * C::HEADB;
+                const uint8_t* vk1 = vk0 + C::HEADB;
+                const uint8_t* vk8 = vk0 + 8 * C::HEADB;
+                const uint8_t* vk9 = vk8 + C::HEADB;
                 const float2 pA = __half22float2(*reinterpret_cast<const __half2*>(&pb0));
                 const float2 pB = __half22float2(*reinterpret_cast<const __half2*>(&pb1));
-                const int vrow = (lane & 7) + 8 * (lane >> 4);
-                const uint32_t vbase = smem_u32(wst);
 #pragma unroll
                 for (int blk = 0; blk < HD / kQK8_0; blk++) {
-                    const float x[4] = {
-                        pA.x * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq) * C::HEADB + blk * kQ8_0Bytes)),
-                        pA.y * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq + 1) * C::HEADB + blk * kQ8_0Bytes)),
-                        pB.x * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq + 8) * C::HEADB + blk * kQ8_0Bytes)),
-                        pB.y * h2f(*reinterpret_cast<const uint16_t*>(vr + (2 * tq + 9) * C::HEADB + blk * kQ8_0Bytes))};
+                    const int db = blk * kQ8_0Bytes;
+                    const float x[4] = {pA.x * h2f(*reinterpret_cast<const uint16_t*>(vk0 + db)),
+                                        pA.y * h2f(*reinterpret_cast<const uint16_t*>(vk1 + db)),
+                                        pB.x * h2f(*reinterpret_cast<const uint16_t*>(vk8 + db)),
+                                        pB.y * h2f(*reinterpret_cast<const uint16_t*>(vk9 + db))};
                     float hi[4], lo[4];
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
@@ -583,10 +637,19 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                     const uint32_t bl0 = pack_h2(lo[0], lo[1]), bl1 = pack_h2(lo[2], lo[3]);
 #pragma unroll
                     for (int n = 2 * blk; n < 2 * blk + 2; n++) {
-                        const int e = n * 16 + 8 * ((lane >> 3) & 1);
+                        const int off = db + 2 + (n & 1) * 16 + 2 * gq;      // dims 16n + 2gq, + 1
+                        // bytes [key k, dim d]: {k0 d0, k0 d1, k1 d0, k1 d1} after the first permute
+                        const uint32_t x01 = __byte_perm(*reinterpret_cast<const uint16_t*>(vk0 + off),
+                                                         *reinterpret_cast<const uint16_t*>(vk1 + off), 0x5410) ^
+                                             0x80808080u;
+                        const uint32_t x89 = __byte_perm(*reinterpret_cast<const uint16_t*>(vk8 + off),
+                                                         *reinterpret_cast<const uint16_t*>(vk9 + off), 0x5410) ^
+                                             0x80808080u;
                         uint32_t af[4];
-                        ldsm_x4_t(vbase + (e / C::COLS) * (16 * C::PITCH) + swz_off(vrow, e % C::COLS, C::PITCH),
-                                  af[0], af[1], af[2], af[3]);
+                        af[0] = u8x2_to_h2<0x4240>(x01);
+                        af[1] = u8x2_to_h2<0x4341>(x01);
+                        af[2] = u8x2_to_h2<0x4240>(x89);
+                        af[3] = u8x2_to_h2<0x4341>(x89);
                         mma_f16(o[n], af, bh0, bh1);
                         mma_f16(o[n], af, bl0, bl1);
                     }
@@ -615,8 +678,13 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
             float* dst = cw + (warp * kRows + r) * C::CW_LD;
 #pragma unroll
             for (int n = 0; n < HD / 16; n++) {
-                dst[n * 16 + gq] = o[n][c];
-                dst[n * 16 + gq + 8] = o[n][c + 2];
+                if constexpr (C::Q8) {   // the V^T M-rows gq, gq + 8 are dims 2gq, 2gq + 1 of the m-tile
+                    dst[n * 16 + 2 * gq] = o[n][c];
+                    dst[n * 16 + 2 * gq + 1] = o[n][c + 2];
+                } else {
+                    dst[n * 16 + gq] = o[n][c];
+                    dst[n * 16 + gq + 8] = o[n][c + 2];
+                }
             }
             if (gq == 0) {
                 cm[warp * kRows + r] = m[c];
@@ -682,64 +750,70 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         consumer_sync();
         if (!*last) return;
         __threadfence();
-        // per (row, split) weights exp2(m_s - M) / L into shared memory (the combine scratch is free)
-        float* wgt = reinterpret_cast<float*>(smem);           // [kRows][ns]
+        // n_g (row, 4-column) groups over the 256 consumer threads: P threads per group, each merging
+        // every P-th split online (running max, rescaled sum) with the (m, l) pairs and partial rows
+        // of 16 splits loaded together, so the whole merge is a few L2 round trips; then the P
+        // partial merges meet in shared memory.
         const size_t tbase = (size_t)kvh * ns * 16;
-        for (int r = warp; r < R; r += kCWarps) {
-            float M = -INFINITY;
-            for (int sp = lane; sp < ns; sp += 32) M = fmaxf(M, __ldcg(&a.ws_ml[(tbase + (size_t)sp * 16 + r) * 2]));
-#pragma unroll
-            for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-            float L = 0.0f;
-            for (int sp = lane; sp < ns; sp += 32) {
-                const float2 ml = __ldcg(reinterpret_cast<const float2*>(&a.ws_ml[(tbase + (size_t)sp * 16 + r) * 2]));
-                const float w = ml.x == -INFINITY ? 0.0f : fast_exp2(ml.x - M);
-                wgt[r * ns + sp] = w;
-                L += ml.y * w;
-            }
-#pragma unroll
-            for (int o2 = 16; o2 > 0; o2 >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o2);
-            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            __syncwarp();
-            for (int sp = lane; sp < ns; sp += 32) wgt[r * ns + sp] *= inv;
-        }
-        consumer_sync();
-        // n_g (row, 4-column) groups over the 256 consumer threads: P threads per group, each summing
-        // every P-th split with eight loads in flight, then the P partial sums meet in shared memory
         const int P = max(1, kCThreads / n_g);
-        float4* part = reinterpret_cast<float4*>(smem + ((R * ns * 4 + 15) & ~15));   // [P][n_g]
+        float4* part_o = reinterpret_cast<float4*>(smem);                   // [P][n_g]
+        float2* part_ml = reinterpret_cast<float2*>(smem + (size_t)P * n_g * sizeof(float4));
         if (tid < P * n_g) {
             const int gi = tid % n_g, sub = tid / n_g;
             const int r = gi / G4, c = (gi % G4) * 4;
+            float M = -INFINITY, L = 0.0f;
             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            int sp = sub;
-            for (; sp + 7 * P < ns; sp += 8 * P) {
-                float4 v[8];
+            for (int sp0 = sub; sp0 < ns; sp0 += 16 * P) {
+                float2 ml[16];
+                float4 v[16];
 #pragma unroll
-                for (int u = 0; u < 8; u++)
-                    v[u] = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[(tbase + (size_t)(sp + u * P) * 16 + r) * HD + c]));
-#pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    const float w = wgt[r * ns + sp + u * P];
-                    acc.x += v[u].x * w; acc.y += v[u].y * w; acc.z += v[u].z * w; acc.w += v[u].w * w;
+                for (int u = 0; u < 16; u++) {
+                    const int sp = sp0 + u * P;
+                    if (sp < ns) {
+                        const size_t slot = tbase + (size_t)sp * 16 + r;
+                        ml[u] = __ldcg(reinterpret_cast<const float2*>(&a.ws_ml[slot * 2]));
+                        v[u] = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[slot * HD + c]));
+                    } else {
+                        ml[u] = make_float2(-INFINITY, 0.0f);
+                    }
                 }
+                float mb = M;
+#pragma unroll
+                for (int u = 0; u < 16; u++) mb = fmaxf(mb, ml[u].x);
+                if (mb == -INFINITY) continue;
+                const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
+                L *= sc;
+                acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+#pragma unroll
+                for (int u = 0; u < 16; u++) {
+                    if (ml[u].x != -INFINITY) {
+                        const float w = fast_exp2(ml[u].x - mb);
+                        L += ml[u].y * w;
+                        acc.x += v[u].x * w; acc.y += v[u].y * w; acc.z += v[u].z * w; acc.w += v[u].w * w;
+                    }
+                }
+                M = mb;
             }
-            for (; sp < ns; sp += P) {
-                const float4 v = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[(tbase + (size_t)sp * 16 + r) * HD + c]));
-                const float w = wgt[r * ns + sp];
-                acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
-            }
-            part[sub * n_g + gi] = acc;
+            part_o[sub * n_g + gi] = acc;
+            part_ml[sub * n_g + gi] = make_float2(M, L);
         }
         consumer_sync();
         for (int gi = tid; gi < n_g; gi += kCThreads) {
             const int r = gi / G4, c = (gi % G4) * 4;
-            float4 acc = part[gi];
-            for (int sub = 1; sub < P; sub++) {
-                const float4 v = part[sub * n_g + gi];
-                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            float M = -INFINITY;
+            for (int sub = 0; sub < P; sub++) M = fmaxf(M, part_ml[sub * n_g + gi].x);
+            float L = 0.0f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sub = 0; sub < P; sub++) {
+                const float2 ml = part_ml[sub * n_g + gi];
+                if (ml.x == -INFINITY) continue;
+                const float w = fast_exp2(ml.x - M);
+                const float4 v = part_o[sub * n_g + gi];
+                L += ml.y * w;
+                acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
             }
-            store_out4<kPeer>(a, kvh, r, c, acc);
+            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+            store_out4<kPeer>(a, kvh, r, c, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
         }
         if (tid == 0) a.tickets[kvh] = 0;
         signal_peers<kPeer>(a, 1, kCThreads);

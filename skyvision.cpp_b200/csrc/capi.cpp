@@ -521,8 +521,14 @@ int sv_attn_append_at(sv_kv* kv, int layer, const void* q, int q_type, const voi
         return SV_ERR_INVALID;
     if (n_head % kv->n_kv_head != 0 || n_head / kv->n_kv_head > 16) return SV_ERR_UNSUPPORTED;
     const int G = n_head / kv->n_kv_head;
-    if (kv->type != SV_TYPE_F16 || T * G > 16) {
-        // the fused kernel covers f16 caches and one query tile; otherwise append, then attend
+    // the fused kernels cover f16 caches with one query tile, and q8_0 caches on the grouped-query
+    // kernel (16-byte aligned f16 sources: each lane quantises 8 elements); otherwise append, then attend
+    const bool src_aligned = ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) & 15) == 0;
+    const bool fused = kv->type == SV_TYPE_F16
+                           ? T * G <= 16
+                           : (kv->type == SV_TYPE_Q8_0 && src_aligned && gqa_enabled() &&
+                              decode_gqa_applies(kv->head_dim, kv->type, T, G, SV_MASK_CAUSAL));
+    if (!fused) {
         int rc = sv_kv_append_at(kv, layer, k_new, v_new, SV_TYPE_F16, T, n_past_dev, stream);
         if (rc != SV_OK) return rc;
         return sv_attn_at(kv, layer, q, q_type, T, n_head, n_past_dev, max_keys, scale, out, stream);

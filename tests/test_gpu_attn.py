@@ -423,6 +423,62 @@ def test_device_npast_graph_replay(orc, fused, NKV, HD, NH):
     assert kv.error_flags() == 0
 
 
+@pytest.mark.parametrize("fused", [True, False])
+def test_device_npast_graph_replay_q8_0(orc, fused):
+    """Config 4's decode step (q8_0 cache, 16q/4kv HD 256, K/V with 1% outliers x8) captured as a
+    CUDA graph and replayed: the appended rows (quantised inside the attention kernel when fused)
+    are bit-exact against the oracle's block_q8_0 rule; attention against the oracle."""
+    NKV, HD, NH, n0, steps = 4, 256, 16, 1500, 4
+    kv = sv.KvCache()
+    assert kv.alloc(0, 2, NKV, HD, 2048, sv.TYPE_Q8_0)
+    for layer in range(2):
+        fill_cache(orc, kv, layer, n0, seed=9 + layer, outliers=0.01)
+    ne0 = NKV * HD
+    q = [orc.normal_f16(9, 400 + i, 2 * NH * HD).reshape(2, 1, NH, HD) for i in range(steps)]
+    k = [orc.normal_f16(9, 500 + i, 2 * ne0, outlier_frac=0.01).reshape(2, 1, ne0) for i in range(steps)]
+    v = [orc.normal_f16(9, 600 + i, 2 * ne0, outlier_frac=0.01).reshape(2, 1, ne0) for i in range(steps)]
+    td = lambda a: torch.from_numpy(a.view(np.float16)).to(DEV)
+    dq, dk, dv = td(q[0]).clone(), td(k[0]).clone(), td(v[0]).clone()
+    dout = torch.zeros(2, 1, NH, HD, dtype=torch.float32, device=DEV)
+    npast = torch.full((1,), n0, dtype=torch.int32, device=DEV)
+    st = torch.cuda.Stream()
+    max_keys = n0 + steps + 3
+
+    def step():
+        for layer in range(2):
+            if fused:
+                kv.attn_append_at(layer, dq[layer], dk[layer], dv[layer], npast, max_keys, 1 / 16.0,
+                                  out=dout[layer], stream=st)
+            else:
+                kv.append_at(layer, dk[layer], dv[layer], npast, stream=st)
+                kv.attn_at(layer, dq[layer], npast, max_keys, 1 / 16.0, out=dout[layer], stream=st)
+        sv.counter_add(npast, 1, stream=st)
+
+    with torch.cuda.stream(st):
+        step()
+        st.synchronize()
+        npast.fill_(n0)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            step()
+        st.synchronize()
+        for i in range(steps):
+            dq.copy_(td(q[i]))
+            dk.copy_(td(k[i]))
+            dv.copy_(td(v[i]))
+            g.replay()
+            st.synchronize()
+            got = dout.cpu().numpy()
+            for layer in range(2):
+                kc = kv.tensor(layer, 0).cpu().numpy()
+                vc = kv.tensor(layer, 1).cpu().numpy()
+                assert np.array_equal(kc[n0 + i], orc.q8_0_quantize(orc.f16_to_f32(k[i][layer, 0])))
+                assert np.array_equal(vc[n0 + i], orc.q8_0_quantize(orc.f16_to_f32(v[i][layer, 0])))
+                close(got[layer], ref_attn(orc, kv, layer, q[i][layer], n0 + i, 1 / 16.0))
+    assert int(npast.item()) == n0 + steps
+    assert kv.error_flags() == 0
+
+
 @pytest.mark.parametrize("fused,NH", [(True, 32), (True, 64), (False, 32)])
 def test_decode_long_context_back_to_back(orc, fused, NH):
     """Many K/V tiles per split (16k keys), several layers, graph replays issued back to back with
