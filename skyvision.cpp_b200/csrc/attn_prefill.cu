@@ -59,15 +59,17 @@ constexpr float kRescaleLog2 = 0.0f;
 // P parts on f16 caches (1: P rounded to f16, standard flash-attention precision)
 constexpr int kF16PParts = 1;
 
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;            // descriptor version (sm100)
-    d |= (uint64_t)2 << 61;            // 128-byte swizzle
-    return d;
+// Shared-memory matrix descriptor (sm100 UMMA): start address >> 4 in bits [0, 14), leading-byte offset
+// >> 4 in [16, 30), stride-byte offset >> 4 in [32, 46), version 1 at bit 46, 128-byte swizzle (2) in
+// [61, 64).
+// Built as (lo, hi) 32-bit words.  The start address (>> 4) occupies the low 14 bits of lo and
+// shared-memory addresses stay below 2^18, so adding (offset >> 4) to lo never carries into the
+// leading-byte-offset field: a k-step's descriptor is its tile's base lo plus a compile-time constant,
+// which keeps the single issuing thread at about one integer add per MMA.
+__device__ __forceinline__ uint32_t desc_lo(uint32_t saddr, uint32_t lbo) {
+    return ((saddr & 0x3FFFFu) >> 4) | (((lbo >> 4) & 0x3FFFu) << 16);
 }
+constexpr uint32_t desc_hi_sw128(uint32_t sbo) { return ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29); }
 
 // kind::f16 instruction descriptor: f32 accumulate, f16 A/B
 __device__ __forceinline__ uint32_t umma_idesc(int M, int N, int a_mn_major, int b_mn_major) {
@@ -75,13 +77,18 @@ __device__ __forceinline__ uint32_t umma_idesc(int M, int N, int a_mn_major, int
            ((uint32_t)(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+// D (+)= A B with both descriptors given as (lo, shared hi) words
+__device__ __forceinline__ void umma_f16_w(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t hi, uint32_t idesc,
+                                           uint32_t acc) {
     asm volatile(
         "{\n"
         ".reg .pred p;\n"
-        "setp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n"
-        "}\n" ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+        ".reg .b64 da, db;\n"
+        "setp.ne.b32 p, %5, 0;\n"
+        "mov.b64 da, {%1, %3};\n"
+        "mov.b64 db, {%2, %3};\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %4, p;\n"
+        "}\n" ::"r"(d_tmem), "r"(a_lo), "r"(b_lo), "r"(hi), "r"(idesc), "r"(acc));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -187,15 +194,17 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
     return __all_sync(0xffffffffu, ok);
 }
 
-// O += P V with P (f16, K-major) read from TMEM
-__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                            uint32_t acc) {
+// O += P V with P (f16, K-major) read from TMEM; B as (lo, hi) descriptor words
+__device__ __forceinline__ void umma_f16_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                              uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n"
         ".reg .pred p;\n"
-        "setp.ne.b32 p, %4, 0;\n"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n"
-        "}\n" ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+        ".reg .b64 db;\n"
+        "setp.ne.b32 p, %5, 0;\n"
+        "mov.b64 db, {%2, %3};\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n"
+        "}\n" ::"r"(d_tmem), "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc));
 }
 
 // Named barrier of the softmax warps.  Code before it may have run on one lane only (a ticket,
@@ -610,7 +619,12 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
         if (lane == 0 && n > 0) {
             const uint32_t idesc_s = umma_idesc(128, C::BN, 0, 0);
             const uint32_t idesc_o = umma_idesc(128, HD, 0, 1);
-            const uint32_t q_base = smem_u32(smem + C::OFF_Q);
+            // descriptor words: K-major Q and K (LBO 16, SBO 1024) and MN-major V (LBO = one 64-column
+            // box, SBO 1024), all 128-byte swizzled, so one hi word serves every operand
+            constexpr uint32_t hi = desc_hi_sw128(1024);
+            const uint32_t q_lo = desc_lo(smem_u32(smem + C::OFF_Q), 16);
+            const uint32_t k_lo = desc_lo(smem_u32(smem + C::OFF_K), 16);
+            const uint32_t v_lo = desc_lo(smem_u32(smem + C::OFF_V), C::KBOX);
             // S(i) = Q K(i)^T into buffer i & 1 of every live Q tile, summed over the NP parts of K(i)
             auto issue_s = [&](int i) -> bool {
                 for (int p = 0; p < NP; p++) {
@@ -618,15 +632,21 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                     if (!wait_or_abort(&full_k[e % C::NEK], (e / C::NEK) & 1, a.err, abort_flag)) return false;
                 }
                 tc_fence_after();
-                for (int q = 0; q < nqt; q++) {
+                uint32_t kd[NP];
+#pragma unroll
+                for (int p = 0; p < NP; p++) kd[p] = k_lo + (uint32_t)(((i * NP + p) % C::NEK) * (C::KV_B >> 4));
+#pragma unroll
+                for (int q = 0; q < NQT; q++) {
+                    if (q >= nqt) break;
+                    const uint32_t d_tmem = tmem + q * C::QCOLS + (i & 1) * C::BN;
 #pragma unroll
                     for (int p = 0; p < NP; p++) {
-                        const uint32_t k_base = smem_u32(smem + C::OFF_K + ((i * NP + p) % C::NEK) * C::KV_B);
 #pragma unroll
                         for (int kk = 0; kk < HD / 16; kk++) {
-                            const uint64_t ad = umma_desc(q_base + q * C::Q_B + (kk / 4) * C::QBOX + (kk % 4) * 32, 16, 1024);
-                            const uint64_t bd = umma_desc(k_base + (kk / 4) * C::KBOX + (kk % 4) * 32, 16, 1024);
-                            umma_f16(tmem + q * C::QCOLS + (i & 1) * C::BN, ad, bd, idesc_s, (kk > 0 || p > 0) ? 1u : 0u);
+                            const uint32_t a_off = (uint32_t)((q * C::Q_B + (kk / 4) * C::QBOX + (kk % 4) * 32) >> 4);
+                            const uint32_t b_off = (uint32_t)(((kk / 4) * C::KBOX + (kk % 4) * 32) >> 4);
+                            umma_f16_w(d_tmem, q_lo + a_off, kd[p] + b_off, hi, idesc_s,
+                                       (kk > 0 || p > 0) ? 1u : 0u);
                         }
                     }
                     umma_commit(&s_full[2 * q + (i & 1)]);
@@ -644,22 +664,25 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                     const int e = i * NP + p;
                     ok = wait_or_abort(&full_v[e % C::NEV], (e / C::NEV) & 1, a.err, abort_flag);
                 }
-                for (int q = 0; q < nqt && ok; q++) {
+                uint32_t vd[NP];
+#pragma unroll
+                for (int p = 0; p < NP; p++) vd[p] = v_lo + (uint32_t)(((i * NP + p) % C::NEV) * (C::KV_B >> 4));
+#pragma unroll
+                for (int q = 0; q < NQT; q++) {
+                    if (q >= nqt || !ok) break;
                     if (!wait_or_abort(&p_full[2 * q + (i & 1)], (i >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
                     tc_fence_after();
                     // f16 P: 8 columns per 16 keys; P_lo (PL = 2) in the next 32 columns
                     const uint32_t p_tmem = tmem + q * C::QCOLS + (i & 1) * C::BN;
+                    const uint32_t o_tmem = tmem + q * C::QCOLS + 128;
 #pragma unroll
                     for (int p = 0; p < NP; p++) {
-                        const uint32_t v_base = smem_u32(smem + C::OFF_V + ((i * NP + p) % C::NEV) * C::KV_B);
 #pragma unroll
                         for (int pp = 0; pp < (p == 0 ? PL : 1); pp++) {   // P_lo meets V's first part only
 #pragma unroll
-                            for (int kk = 0; kk < C::BN / 16; kk++) {
-                                const uint64_t bd = umma_desc(v_base + kk * 16 * 128, C::KBOX, 1024);
-                                umma_f16_ts(tmem + q * C::QCOLS + 128, p_tmem + pp * 32 + kk * 8, bd, idesc_o,
-                                            (i > 0 || p > 0 || pp > 0 || kk > 0) ? 1u : 0u);
-                            }
+                            for (int kk = 0; kk < C::BN / 16; kk++)
+                                umma_f16_ts_w(o_tmem, p_tmem + pp * 32 + kk * 8, vd[p] + (uint32_t)(kk * 16 * 128 >> 4), hi,
+                                              idesc_o, (i > 0 || p > 0 || pp > 0 || kk > 0) ? 1u : 0u);
                         }
                     }
                     umma_commit(&o_done[2 * q + (i & 1)]);
