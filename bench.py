@@ -763,7 +763,7 @@ def check_flags(kv, stream=None):
 def run_kernels(args):
     """Each kernel of the path on a small single-layer case, 3 launches each in this order:
     fused decode (config 2 geometry, S = 4481), windowed decode (2 sessions of ~19k rows),
-    chunked prefill (384 over 4096), f16 and q8_0 append, compaction, q8_0 decode and the last q8_0
+    chunked prefill (384 over 4096), f16 and q8_0 append, compaction, fused q8_0 decode and the last q8_0
     prefill chunk (config 4 geometry: q8_0_split_kernel, then the tensor-core kernel on hi + lo parts).  Under 1 GB on the device; used by the committed ncu summaries."""
     import torch
     from __graft_entry__ import load_package
@@ -816,7 +816,8 @@ def run_kernels(args):
         kq.append(0, kt4, kt4, base=c * 512)
     npq = torch.full((1,), 8192, dtype=torch.int32, device=dev)
     q4 = torch.randn(1, 16, 256, generator=g, device=dev).half()
-    timed("decode_q8_0_us", lambda: kq.attn_at(0, q4, npq, 8193, 1 / 16.0))
+    k4 = torch.randn(1, 1024, generator=g, device=dev).half()
+    timed("decode_q8_0_us", lambda: kq.attn_append_at(0, q4, k4, k4, npq, 8193, 1 / 16.0))
     q5 = torch.randn(512, 16, 256, generator=g, device=dev).half()
     timed("prefill_q8_0_us", lambda: kq.attn(0, q5, n_past=8192 - 512, scale=1 / 16.0))
     torch.cuda.synchronize()
