@@ -9,7 +9,7 @@
 // Work unit: NQT query tiles of 128 rows (NQT = 2 at HD 128 when the chunk has two) x one kv
 // head x one split of its keys.  A tile's 128 rows pack 128/G queries x the G query heads of the
 // kv head, so every K/V tile feeds all heads of the GQA group, and with NQT = 2 each K/V tile
-// read from L2 feeds 256 rows.  Warp roles ((4*NQT + 2) warps):
+// read from L2 feeds 256 rows.  Warp roles ((4*NQT + 3) warps):
 //   softmax warps (4 per query tile; warp w reads TMEM lane quarter w % 4, one row per thread):
 //              per 64-key tile read S (64 columns) with tcgen05.ld, apply scale and the causal
 //              predicate, take the row max, write P = exp2(S - m) as f16 over the first 32
@@ -17,10 +17,12 @@
 //              row max grew, rescale the row of O in TMEM after the exponentials (which overlap
 //              the previous tile's P.V).  One exponential in four runs on the FMA pipe
 //              (exp2_fma) to take load off the SFU.
-//   TMA warp   lane 0 loads the query tiles (a 3D map over [T][NH][HD] whose {64, G, 128/G} box
-//              is one slab of a tile) and streams K tiles, lane 1 V tiles, each into its own ring
-//              (5 stages at HD 128, 2 at HD 256); a K stage is refilled as soon as its S has
-//              completed, a V stage after its P.V.
+//   TMA warps  one lane of the first loads the query tiles (a 3D map over [T][NH][HD] whose
+//              {64, G, 128/G} box is one slab of a tile) and streams K tiles, one lane of the second
+//              V tiles, each into its own ring (5 stages at HD 128, 2 at HD 256); a K stage is
+//              refilled as soon as its S has completed, a V stage after its P.V.  The two rings have
+//              a warp each: as two lanes of one warp, a V lane blocked in its slot wait held back the
+//              K lane's loads (~450 cycles of the MMA thread's wait per tile, in-kernel stamps).
 //   MMA warp   (one thread) S double-buffered in TMEM per query tile, so the tensor core computes
 //              S(j+1) while the softmax warps work on S(j):
 //                S  = Q K^T   M=128, N=64 keys, K=HD   (A, B K-major, shared memory)
@@ -170,7 +172,7 @@ struct PreCfg {
     static constexpr int TMEM_COLS = NQT * QCOLS <= 256 ? 256 : 512;
     static_assert(NQT * QCOLS <= 512, "TMEM budget");
     static constexpr int SM_WARPS = 4 * NQT;              // softmax warps: one row per thread
-    static constexpr int THREADS = (SM_WARPS + 2) * 32;   // + TMA producer warp + MMA warp
+    static constexpr int THREADS = (SM_WARPS + 3) * 32;   // + K and V producer warps + MMA warp
     static constexpr int ROWS = NQT * 128;
 };
 
@@ -226,7 +228,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                   const __grid_constant__ CUtensorMap tmq, const __grid_constant__ AttnArgs a) {
     using C = PreCfg<HD, NQT, NP>;
     constexpr int kSoftmaxWarps = C::SM_WARPS;
-    constexpr int kTmaWarp = kSoftmaxWarps;   // then one MMA-issuer warp
+    constexpr int kTmaWarp = kSoftmaxWarps;   // Q and K producer; then the V producer and the MMA issuer
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -578,9 +580,11 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                 }
             }
         }
-    } else if (warp == kTmaWarp) {
-        // ============================ TMA producers: lane 0 loads the Q tiles, then streams K tiles; lane 1 V
-        if (lane == 0 && a.q_tma) {
+    } else if (warp == kTmaWarp || warp == kTmaWarp + 1) {
+        // ============================ TMA producers: lane 0 of the first warp loads the Q tiles, then
+        // streams K tiles; lane 0 of the second streams V tiles
+        const bool is_v = warp == kTmaWarp + 1;
+        if (!is_v && lane == 0 && a.q_tma) {
             // box {64 columns, G heads, QPT queries} = the 128 rows of a Q tile in row order qi*G + g
             mbar_arrive_expect_tx(q_full, (uint32_t)(nqt * C::Q_B));
             for (int q = 0; q < nqt; q++)
@@ -588,9 +592,8 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                 for (int b = 0; b < HD / 64; b++)
                     tma_load_3d(smem + C::OFF_Q + q * C::Q_B + b * C::QBOX, &tmq, b * 64, kvh * a.G, t0 + q * QPT, q_full);
         }
-        if (lane < 2 && n > 0) {
+        if (lane == 0 && n > 0) {
             // ring entries in the order the MMA warp consumes them: tile i, part p -> entry i*NP + p
-            const bool is_v = lane == 1;
             uint64_t* fullx = is_v ? full_v : full_k;
             uint64_t* emptyx = is_v ? empty_v : empty_k;
             const int NE = is_v ? C::NEV : C::NEK;
@@ -613,7 +616,7 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                 mbar_wait(&fullx[e % NE], (e / NE) & 1, a.err);
         }
         // never leave the Q copy in flight either (a CTA without keys does not wait for it otherwise)
-        if (lane == 0 && a.q_tma) mbar_wait(q_full, 0, a.err);
+        if (!is_v && lane == 0 && a.q_tma) mbar_wait(q_full, 0, a.err);
     } else {
         // ============================ MMA issuer
         if (lane == 0 && n > 0) {
@@ -769,11 +772,14 @@ cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensor
                       NP == 2 ? *tk2 : *tk, NP == 2 ? *tv2 : *tv, tq, a);
 }
 
-// q8_0 rows -> f16 (hi, lo) parts for the tensor-core prefill.  x = q * d is exact in f32 (an 8-bit
-// integer times an 11-bit significand); hi = f16(x) and lo = f16(x - hi) (x - hi is exact in f32 and
-// has at most 8 significant bits), so hi + lo = x, the value the oracle's dequantisation gives, up
-// to f16 subnormal rounding of lo (< 2^-25).  One thread per 8 elements of one row of K or V;
-// planes[0..3] = K hi, K lo, V hi, V lo, each [row][ne0] f16.
+// q8_0 rows -> f16 (hi, lo) parts for the tensor-core prefill.  With q an 8-bit integer and d the
+// block's f16 scale, hi = f16(q * d) and lo = f16(q * d - hi) (q * d - hi has at most 8 significant
+// bits), so hi + lo = q * d, the value the oracle's dequantisation gives, up to f16 subnormal
+// rounding of lo (< 2^-25).  Computed in f16 arithmetic, off the conversion pipe: q becomes an exact
+// f16 integer by byte permutes (0x64uu = 1024 + u, u = q + 128, minus 1152), hi = HMUL2(q, d) is
+// the single round-to-nearest of the exact product, and lo = HFMA2(q, d, -hi) rounds q * d - hi once.
+// One thread per 8 elements of one row of K or V; planes[0..3] = K hi, K lo, V hi, V lo, each
+// [row][ne0] f16.
 __global__ void __launch_bounds__(256) q8_0_split_kernel(const uint8_t* __restrict__ kc, const uint8_t* __restrict__ vc,
                                                          size_t row_bytes, int ne0, int n_rows, uint16_t* planes,
                                                          size_t plane_elems) {
@@ -785,17 +791,19 @@ __global__ void __launch_bounds__(256) q8_0_split_kernel(const uint8_t* __restri
     const int row = (int)(idx / per_row), e = (int)(idx % per_row) * 8;
     const int is_v = blockIdx.y;
     const uint8_t* blk = (is_v ? vc : kc) + (size_t)row * row_bytes + (size_t)(e / kQK8_0) * kQ8_0Bytes;
-    const float d = h2f(*reinterpret_cast<const uint16_t*>(blk));
+    const __half2 d2 = __half2half2(__ushort_as_half(__ldg(reinterpret_cast<const uint16_t*>(blk))));
     const uint16_t* qs = reinterpret_cast<const uint16_t*>(blk + 2 + (e % kQK8_0));   // 2-byte aligned
+    const __half2 k1152 = __half2half2(__ushort_as_half(0x6480u));
     uint32_t hi[4], lo[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const uint16_t w = __ldg(qs + i);
-        const float x0 = (float)(int8_t)(w & 0xff) * d, x1 = (float)(int8_t)(w >> 8) * d;
-        const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-        const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
-        hi[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-        lo[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        const uint32_t u = (uint32_t)__ldg(qs + i) ^ 0x8080u;
+        const uint32_t hq = __byte_perm(u, 0x64646464u, 0x4140);   // {1024 + u0, 1024 + u1}
+        const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&hq), k1152);
+        const __half2 h = __hmul2(q, d2);
+        const __half2 l = __hfma2(q, d2, __hneg2(h));
+        hi[i] = *reinterpret_cast<const uint32_t*>(&h);
+        lo[i] = *reinterpret_cast<const uint32_t*>(&l);
     }
     uint16_t* dst = planes + (size_t)(2 * is_v) * plane_elems + (size_t)row * ne0 + e;
     *reinterpret_cast<uint4*>(dst) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
