@@ -268,6 +268,26 @@ int sv_session_end_turn(sv_session* s, int frames, int text_rows, int answer_row
  * compacted) row id of cache row i, i < *n_rows (max_rows caps the copy). */
 int sv_session_rows(const sv_session* s, int* n_rows, int64_t* rows_out, int max_rows);
 
+/* Row-budget sessions (MossVL's streaming self-KV, moss_vl_model.cpp:250-292):
+ * the cache holds a pinned sink prefix and a sliding window of rows, with no
+ * turn table (these calls return SV_ERR_INVALID once sv_session_begin_turn has
+ * been used, until sv_session_reset).
+ *
+ * sv_session_make_room replaces session_compact_self (moss_vl_model.cpp:275-292):
+ * before `need` new rows are written, if rows + need exceed the capacity
+ * (capacity rows, or the cache's n_ctx when 0), the oldest rows after the sink
+ * leave in multiples of 128, never touching the newest 256 rows; the survivors
+ * move down in place (sv_kv_compact, every layer's K and V) instead of the
+ * reference's host round trip per tensor (kv_shift_rows, :264-271).
+ * *evicted gets the rows removed now, *rope_shift the total removed since the
+ * reset, which the caller adds to a new row's slot to get its rope position
+ * (the reference's sess_rdelta += evict, :287).  SV_ERR_OVERFLOW when even the
+ * largest eviction cannot make room (the reference's `false`).  Either pointer
+ * may be NULL. */
+int sv_session_make_room(sv_session* s, int need, int capacity, int* evicted, int64_t* rope_shift, void* stream);
+/* Record n rows written after the current rows (n_past += n in the reference). */
+int sv_session_push_rows(sv_session* s, int n);
+
 /* ---------------------------------------------------------------- head-sharded decode, gather fused in
  * One session too long for one GPU's bandwidth shards by kv head (rank g holds kv heads
  * [g*NKV/G, (g+1)*NKV/G) and their query heads).  The reference-side design gathers each layer's

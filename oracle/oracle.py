@@ -279,6 +279,41 @@ class SessionRows:
         return np.array(out, dtype=np.int64)
 
 
+class RowBudgetSession:
+    """MossVL's streaming self-KV budget (moss_vl_model.cpp:250-292), restated on a row-id list.
+
+    rows[i] is the original id of cache row i; rows [0, sink) are pinned.  make_room(need, n_ctx)
+    follows session_compact_self (:275-292): nothing happens while n_past + need fits; otherwise
+    needed_free = n_past + need - n_ctx, evictable = n_past - sink - 256 (recent_floor, :278), and
+    evict = min(evictable, needed_free rounded up to 128) rows right after the sink leave
+    (kv_shift_rows moves the rest down, :282-285), n_past -= evict, rdelta += evict (:287).  Returns
+    the eviction count, or None where the reference returns false (evictable < needed_free).
+    """
+
+    def __init__(self, sink_rows: int = 0):
+        self.sink = sink_rows
+        self.rows = list(range(sink_rows))
+        self.next_id = sink_rows
+        self.rdelta = 0
+
+    def make_room(self, need: int, n_ctx: int):
+        n_past = len(self.rows)
+        if n_past + need <= n_ctx:
+            return 0
+        needed_free = n_past + need - n_ctx
+        evictable = n_past - self.sink - 256
+        if evictable < needed_free:
+            return None
+        evict = min(evictable, (needed_free + 127) // 128 * 128)
+        del self.rows[self.sink:self.sink + evict]
+        self.rdelta += evict
+        return evict
+
+    def push(self, n: int) -> None:
+        self.rows += list(range(self.next_id, self.next_id + n))
+        self.next_id += n
+
+
 def compact_rows(cache: np.ndarray, keep, dst_base: int) -> None:
     """Order-preserving in-place move of kept rows to dst_base.. (moss_vl kv_shift_rows)."""
     k = np.ascontiguousarray(keep, dtype=np.int32)

@@ -113,6 +113,8 @@ def lib() -> ctypes.CDLL:
         "sv_session_begin_turn": (I, [P, I, ctypes.POINTER(I), ctypes.POINTER(I), P]),
         "sv_session_end_turn": (I, [P, I, I, I]),
         "sv_session_rows": (I, [P, ctypes.POINTER(I), P, I]),
+        "sv_session_make_room": (I, [P, I, I, ctypes.POINTER(I), ctypes.POINTER(ctypes.c_int64), P]),
+        "sv_session_push_rows": (I, [P, I]),
         "sv_selftest_wait_timeout": (I, [P, P, ctypes.c_uint, P]),
         "sv_peer_create": (I, [I, I, I, I, SZ, ctypes.POINTER(P)]),
         "sv_peer_export": (I, [P, P]),
@@ -462,6 +464,19 @@ class Session:
 
     def end_turn(self, frames: int, text_rows: int, answer_rows: int) -> None:
         _check("sv_session_end_turn", lib().sv_session_end_turn(self.h, frames, text_rows, answer_rows))
+
+    def make_room(self, need: int, capacity: int = 0, stream=None):
+        """Row-budget eviction before `need` new rows (MossVL's session_compact_self): returns
+        (rows evicted now, total rope-position shift since the reset)."""
+        ev = ctypes.c_int()
+        shift = ctypes.c_int64()
+        st = _stream(stream) if self.kv is not None else None
+        _check("sv_session_make_room", lib().sv_session_make_room(self.h, need, capacity, ctypes.byref(ev),
+                                                                  ctypes.byref(shift), st))
+        return ev.value, shift.value
+
+    def push_rows(self, n: int) -> None:
+        _check("sv_session_push_rows", lib().sv_session_push_rows(self.h, n))
 
     def rows(self):
         import numpy as np

@@ -12,7 +12,13 @@
 //     mechanism, moss_vl_model.cpp:264-291) and the new turn is appended after
 //     the surviving rows, which keep their original positions (the caller's
 //     rope positions are unchanged, as moss_vl's sess_rdelta does);
-//   * the splice predicate (qwen3vl_model.cpp:1165-1171).
+//   * the splice predicate (qwen3vl_model.cpp:1165-1171);
+//   * the row-budget eviction of MossVL's streaming session (session_compact_self,
+//     moss_vl_model.cpp:273-292): before n new rows are written into a full cache, the oldest rows
+//     after the pinned sink prefix leave in 128-row quanta, never reaching into the newest 256
+//     rows, the survivors move down in place (sv_kv_compact) and the eviction count accumulates
+//     into the rope-position shift (the reference's sess_rdelta), so every surviving row keeps
+//     its original position.
 #include <algorithm>
 #include <cstdio>
 #include <vector>
@@ -37,6 +43,7 @@ struct sv_session {
     int n_marks = 0;                   // retained frames incl. the open turn's
     bool open = false;
     int open_frames = 0;
+    int64_t rope_shift = 0;            // rows evicted by sv_session_make_room since the last reset
 };
 
 namespace {
@@ -49,7 +56,12 @@ void reset_rows(sv_session* s) {
     s->n_marks = 0;
     s->open = false;
     s->open_frames = 0;
+    s->rope_shift = 0;
 }
+
+// MossVL's session_compact_self constants (moss_vl_model.cpp:278, 281)
+constexpr int kRecentFloor = 256;   // the newest rows are never evicted
+constexpr int kEvictQuantum = 128;  // evictions are rounded up to whole quanta
 
 }  // namespace
 
@@ -168,6 +180,40 @@ int sv_session_end_turn(sv_session* s, int frames, int text_rows, int answer_row
     for (int r = 0; r < rows; r++) s->row_ids.push_back(s->next_id++);
     s->turns.push_back(t);
     s->open = false;
+    return SV_OK;
+}
+
+int sv_session_make_room(sv_session* s, int need, int capacity, int* evicted, int64_t* rope_shift, void* stream) {
+    if (evicted) *evicted = 0;
+    if (!s || need < 0 || capacity < 0 || s->open || !s->turns.empty()) return SV_ERR_INVALID;
+    const int cap = capacity > 0 ? capacity : (s->kv ? s->kv->n_ctx : 0);
+    if (cap <= 0 || (s->kv && cap > s->kv->n_ctx)) return SV_ERR_INVALID;
+    const int n_past = (int)s->row_ids.size();
+    if (rope_shift) *rope_shift = s->rope_shift;
+    if (n_past + need <= cap) return SV_OK;
+    const int needed_free = n_past + need - cap;
+    const int evictable = n_past - s->sink_rows - kRecentFloor;
+    if (evictable < needed_free) return SV_ERR_OVERFLOW;
+    const int evict = std::min(evictable, (needed_free + kEvictQuantum - 1) / kEvictQuantum * kEvictQuantum);
+    const int tail = n_past - s->sink_rows - evict;
+    if (s->kv) {
+        const sv_segment segs[3] = {{0, s->sink_rows, 1}, {s->sink_rows, evict, 0}, {s->sink_rows + evict, tail, 1}};
+        int new_len = 0;
+        const int rc = sv_kv_compact(s->kv, segs, 3, 0, &new_len, stream);
+        if (rc != SV_OK) return rc;
+    }
+    s->row_ids.erase(s->row_ids.begin() + s->sink_rows, s->row_ids.begin() + s->sink_rows + evict);
+    s->rope_shift += evict;
+    if (evicted) *evicted = evict;
+    if (rope_shift) *rope_shift = s->rope_shift;
+    fprintf(stderr, "session: evicted %d rows (sink %d, live %d)\n", evict, s->sink_rows, n_past - evict);
+    return SV_OK;
+}
+
+int sv_session_push_rows(sv_session* s, int n) {
+    if (!s || n < 0 || s->open || !s->turns.empty()) return SV_ERR_INVALID;
+    if (s->kv && (int64_t)s->row_ids.size() + n > s->kv->n_ctx) return SV_ERR_OVERFLOW;
+    for (int r = 0; r < n; r++) s->row_ids.push_back(s->next_id++);
     return SV_OK;
 }
 

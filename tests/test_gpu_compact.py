@@ -117,3 +117,48 @@ def test_session_config3_shape(orc):
             k, v = written[(layer, int(rid))]
             assert np.array_equal(kc[i], k) and np.array_equal(vc[i], v), (layer, i, rid)
     assert kv.error_flags() == 0
+
+
+def test_session_row_budget_stream(orc):
+    """MossVL-style streaming (pinned sink + sliding window, moss_vl_model.cpp:250-292) on a real
+    cache: rows are appended in bursts, sv_session_make_room evicts in 128-row quanta before each
+    burst, and every layer's K and V must hold exactly the oracle's surviving rows in order."""
+    rng = np.random.default_rng(7)
+    L, NKV, HD, cap, sink = 2, 4, 64, 2048, 40
+    kv = sv.KvCache()
+    assert kv.alloc(0, L, NKV, HD, cap)
+    sess = sv.Session(kv, max_frames=1, rows_per_frame=1, sink_rows=sink)
+    ref = orc.RowBudgetSession(sink)
+    ne0 = NKV * HD
+    # every written row carries its row id as the bit pattern of all its elements (K: id, V: id + 15000,
+    # both below the f16 inf/nan patterns), so the cache shows exactly which rows survive
+    def write(first_slot, ids):
+        bits = np.repeat(np.asarray(ids, np.int16)[:, None], ne0, axis=1)
+        kb = torch.from_numpy(bits).to(DEV).view(torch.float16)
+        vb = torch.from_numpy(bits + np.int16(15000)).to(DEV).view(torch.float16)
+        for layer in range(L):
+            kv.append(layer, kb, vb, base=first_slot)
+    write(0, list(range(sink)))
+    shift_total = 0
+    for burst in range(40):
+        need = int(rng.integers(20, 400))
+        want = ref.make_room(need, cap)
+        assert want is not None
+        ev, shift = sess.make_room(need)
+        assert ev == want and shift == ref.rdelta
+        shift_total = shift
+        n_past = len(ref.rows)
+        write(n_past, list(range(ref.next_id, ref.next_id + need)))
+        sess.push_rows(need)
+        ref.push(need)
+    torch.cuda.synchronize()
+    rows = np.array(ref.rows)
+    assert np.array_equal(sess.rows(), rows)
+    assert shift_total > 0
+    want = np.repeat(rows.astype(np.int16)[:, None], ne0, axis=1)
+    for layer in range(L):
+        k = kv.tensor(layer, 0).view(torch.int16)[: rows.size].cpu().numpy()
+        v = kv.tensor(layer, 1).view(torch.int16)[: rows.size].cpu().numpy()
+        assert np.array_equal(k, want)
+        assert np.array_equal(v, want + np.int16(15000))
+    assert kv.error_flags() == 0

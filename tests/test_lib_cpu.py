@@ -91,6 +91,42 @@ def test_session_random_turns(seed, orc):
     _drive(sess, ref, turns[:5])
 
 
+@pytest.mark.parametrize("seed", range(6))
+def test_session_row_budget_random(seed, orc):
+    """MossVL's row-budget eviction (session_compact_self) on a host-only session against the
+    oracle's restatement: eviction counts, the rope-position shift and the kept-row map."""
+    rng = np.random.default_rng(100 + seed)
+    sink = int(rng.integers(0, 64))
+    n_ctx = int(rng.integers(sink + 400, 4096))
+    sess = sv.Session(None, max_frames=1, rows_per_frame=1, sink_rows=sink)
+    ref = orc.RowBudgetSession(sink)
+    for _ in range(60):
+        need = int(rng.integers(1, 700))
+        want = ref.make_room(need, n_ctx)
+        if want is None:                       # the reference refuses: context overflow
+            with pytest.raises(sv.SvError) as ex:
+                sess.make_room(need, n_ctx)
+            assert ex.value.status == -5          # SV_ERR_OVERFLOW
+            break
+        ev, shift = sess.make_room(need, n_ctx)
+        assert ev == want and shift == ref.rdelta
+        sess.push_rows(need)
+        ref.push(need)
+        assert np.array_equal(sess.rows(), np.array(ref.rows, dtype=np.int64))
+
+
+def test_session_row_budget_refuses_turn_sessions():
+    sess = sv.Session(None, max_frames=4, rows_per_frame=2)
+    sess.begin_turn(1)
+    with pytest.raises(sv.SvError):
+        sess.make_room(10, 100)
+    sess.end_turn(1, 3, 2)
+    with pytest.raises(sv.SvError):
+        sess.push_rows(5)
+    sess.reset()
+    assert sess.make_room(10, 100) == (0, 0)
+
+
 def test_create_without_gpu_reports_status():
     import torch
     if torch.cuda.is_available():
