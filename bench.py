@@ -421,7 +421,7 @@ def run_svkv(args, world, rank, local):
     batched = None if args.no_batched else run_batched(sv, dev, stream, rank, world, K, W)
     extras = {}
     if world == 1 and not args.no_batched:
-        for name, fn in (("config3_eviction", run_cfg3), ("config4_q8_0", run_cfg4)):
+        for name, fn in (("config3_eviction", run_cfg3), ("config4_q8_0", run_cfg4), ("qk_norm_rope_append", run_rope)):
             try:
                 extras[name] = fn(sv, dev, stream)
             except Exception as ex:          # an extra leg never takes the headline line down
@@ -754,6 +754,57 @@ def run_cfg4(sv, dev, stream):
     }
 
 
+def run_rope(sv, dev, stream):
+    """The step before the append, fused (sv_qk_norm_rope_append): per-head q/k RMSNorm * weight,
+    Qwen3-VL interleaved MRoPE (theta 5e6, sections 24/20/20/0, four position streams) and the K/V
+    append, on config 2's geometry over 36 layers (one CUDA graph of 36 launches): the 384-token splice
+    tail and one decode token.  HBM-bound; algorithmic bytes per launch = f32 q, k, v read + f16 q_out
+    and K/V rows written."""
+    import torch
+    out = {"workload": "config 2 geometry (32q/8kv HD 128, f16 cache), 36 layers, IMROPE 24/20/20/0, eps 1e-6"}
+    kv = sv.KvCache()
+    assert kv.alloc(dev.index, L, NKV, HD, CAP)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    qn = 1.0 + 0.1 * torch.randn(HD, generator=gen, device=dev)
+    kn = 1.0 + 0.1 * torch.randn(HD, generator=gen, device=dev)
+    rope = (sv.ROPE_IMROPE, HD, 5e6, (24, 20, 20, 0))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for T, base, reps in ((TAIL, PRE, 20), (1, PRE + TAIL, 50)):
+            q = torch.randn(L, T, NH, HD, generator=gen, device=dev)
+            k = torch.randn(L, T, NKV, HD, generator=gen, device=dev)
+            v = torch.randn(L, T, NKV, HD, generator=gen, device=dev)
+            pos = torch.stack([torch.arange(base, base + T, device=dev)] * 4).to(torch.int32).contiguous()
+            qo = torch.empty(L, T, NH, HD, dtype=torch.float16, device=dev)
+
+            def layers():
+                for layer in range(L):
+                    kv.norm_rope_append(layer, q[layer], k[layer], v[layer], pos, rope=rope, q_norm=qn, k_norm=kn,
+                                        eps=1e-6, base=base, q_out=qo[layer], stream=stream)
+
+            layers()
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()          # 36 launches per replay, no host work in between
+            with torch.cuda.graph(g, stream=stream):
+                layers()
+            g.replay()
+            stream.synchronize()
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+            del g
+            us = e0.elapsed_time(e1) * 1e3 / (reps * L)
+            nbytes = T * (NH + 2 * NKV) * HD * 4 + T * NH * HD * 2 + 2 * T * NKV * HD * 2
+            out[f"T{T}_us_per_layer"] = us
+            out[f"T{T}_gbs"] = nbytes / (us * 1e-6) / 1e9
+        check_flags(kv, stream)
+    kv.free()
+    return out
+
+
 def check_flags(kv, stream=None):
     """Device error bits of a cache handle (row range, expired wait, bad segment) must be clear."""
     f = kv.error_flags(stream=stream)
@@ -764,7 +815,9 @@ def run_kernels(args):
     """Each kernel of the path on a small single-layer case, 3 launches each in this order:
     fused decode (config 2 geometry, S = 4481), windowed decode (2 sessions of ~19k rows),
     chunked prefill (384 over 4096), f16 and q8_0 append, compaction, fused q8_0 decode and the last q8_0
-    prefill chunk (config 4 geometry: q8_0_split_kernel, then the tensor-core kernel on hi + lo parts).  Under 1 GB on the device; used by the committed ncu summaries."""
+    prefill chunk (config 4 geometry: q8_0_split_kernel, then the tensor-core kernel on hi + lo parts), and
+    the fused q/k norm + IMROPE + append of a config 2 splice tail (384 tokens).  Under 1 GB on the
+    device; used by the committed ncu summaries."""
     import torch
     from __graft_entry__ import load_package
     sv = load_package()
@@ -820,6 +873,12 @@ def run_kernels(args):
     timed("decode_q8_0_us", lambda: kq.attn_append_at(0, q4, k4, k4, npq, 8193, 1 / 16.0))
     q5 = torch.randn(512, 16, 256, generator=g, device=dev).half()
     timed("prefill_q8_0_us", lambda: kq.attn(0, q5, n_past=8192 - 512, scale=1 / 16.0))
+    qr = torch.randn(TAIL, NH, HD, generator=g, device=dev)
+    kr = torch.randn(TAIL, NKV, HD, generator=g, device=dev)
+    pr = torch.stack([torch.arange(PRE, PRE + TAIL, device=dev)] * 4).to(torch.int32).contiguous()
+    wr = torch.ones(HD, device=dev)
+    timed("norm_rope_append_us", lambda: kv.norm_rope_append(0, qr, kr, kr, pr, rope=(sv.ROPE_IMROPE, HD, 5e6, (24, 20, 20, 0)),
+                                                             q_norm=wr, k_norm=wr, base=PRE))
     torch.cuda.synchronize()
     assert kv.error_flags() == 0 and kq.error_flags() == 0 and kw.error_flags() == 0
     print(json.dumps({"workload": "kernels", "us_per_launch": times}), flush=True)

@@ -268,6 +268,43 @@ int sv_session_end_turn(sv_session* s, int frames, int text_rows, int answer_row
  * compacted) row id of cache row i, i < *n_rows (max_rows caps the copy). */
 int sv_session_rows(const sv_session* s, int* n_rows, int64_t* rows_out, int max_rows);
 
+/* ---------------------------------------------------------------- q/k norm + RoPE fused into the append
+ * Rotary modes, ggml's type ids: NEOX rotates pairs (i, i + n_dims/2) at one position per token
+ * (ggml_rope_ext, e.g. gemma4_model.cpp:640-642); IMROPE is Qwen3-VL's interleaved multi-axis
+ * form (ggml_rope_multi with GGML_ROPE_TYPE_IMROPE, qwen3vl_model.cpp:644-650): pair i takes its
+ * position from stream h when i % 3 == 1 and i < 3*sections[1], from w when i % 3 == 2 and
+ * i < 3*sections[2], from t when i % 3 == 0 and i < 3*sections[0], else from the fourth stream
+ * (i counted modulo the section sum), with NEOX pairing. */
+#define SV_ROPE_NONE 0
+#define SV_ROPE_NEOX 2
+#define SV_ROPE_IMROPE 40
+
+typedef struct sv_rope {
+    int mode;          /* SV_ROPE_NONE / SV_ROPE_NEOX / SV_ROPE_IMROPE */
+    int n_dims;        /* rotated dims: head_dim, or head_dim / 2 for head_dim 128 / 256 */
+    float freq_base;   /* theta = pos * freq_base^(-2i / n_dims) */
+    int sections[4];   /* IMROPE: t, h, w, extra pair counts (Qwen3-VL: 24, 20, 20, 0) */
+} sv_rope;
+
+/* The ops of a decoder layer between the QKV projection and the attention
+ * (qwen3vl_model.cpp:636-655): per-head RMSNorm of q and k times their weights
+ * (ggml_rms_norm + ggml_mul; q_norm / k_norm NULL = no norm, eps as
+ * rms_norm_eps), the rotary embedding of q and k, and ggml_set_rows of k and
+ * v into the cache at rows slot_base + t (or *slot_base_dev + t when
+ * slot_base_dev is set, graph-stable like sv_kv_append_at), in one launch.
+ * q, k, v: device f32 [T][n_head | n_kv_head][head_dim] (the projections'
+ * outputs); pos: device int32 [T] (NEOX) or [4][T] (IMROPE: t, h, w, extra
+ * streams, the reference's mpos layout, qwen3vl_model.cpp:602-605);
+ * rope NULL or mode SV_ROPE_NONE = no rotation.  q_out gets the rotated
+ * queries, [T][n_head][head_dim] in q_out_type (SV_TYPE_F16 or SV_TYPE_F32),
+ * for sv_attn*.  Cache rows are f16 (RNE) or q8_0 with sv_set_rows's exact
+ * quantisation.  head_dim 64 / 128 / 256.  A row outside the cache is not
+ * written and sets the device error bit SV_DEVERR_ROW_RANGE. */
+int sv_qk_norm_rope_append(sv_kv* kv, int layer, const float* q, const float* k, const float* v, int T, int n_head,
+                           const float* q_norm, const float* k_norm, float eps, const sv_rope* rope,
+                           const int32_t* pos, int slot_base, const int32_t* slot_base_dev, void* q_out,
+                           int q_out_type, void* stream);
+
 /* Row-budget sessions (MossVL's streaming self-KV, moss_vl_model.cpp:250-292):
  * the cache holds a pinned sink prefix and a sliding window of rows, with no
  * turn table (these calls return SV_ERR_INVALID once sv_session_begin_turn has

@@ -202,6 +202,66 @@ def soft_max_row(x, mask=None, scale: float = 1.0) -> np.ndarray:
     return y
 
 
+# ----------------------------------------------------------------- q/k norm + rotary embedding
+ROPE_NONE, ROPE_NEOX, ROPE_IMROPE = 0, 2, 40
+
+
+def rms_norm(x, w, eps: float) -> np.ndarray:
+    """ggml_rms_norm over the last axis, then ggml_mul by w (qwen3vl_model.cpp:638-642), in float64:
+    y = x / sqrt(mean(x^2) + eps) * w (the reference's numpy form, scripts/parity_minicpmo_seg.py:29-30)."""
+    x = np.asarray(x, np.float64)
+    return x / np.sqrt((x * x).mean(-1, keepdims=True) + eps) * np.asarray(w, np.float64)
+
+
+def imrope_axis(i: int, sections) -> int:
+    """Position stream of rotation pair i in ggml's interleaved MRoPE (GGML_ROPE_TYPE_IMROPE, the
+    Qwen3-VL rope of qwen3vl_model.cpp:644-650; ggml-cpu's mrope cache rule, ggml-org/ggml master):
+    h when i % 3 == 1 and i < 3*s[1], w when i % 3 == 2 and i < 3*s[2], t when i % 3 == 0 and
+    i < 3*s[0], else the fourth stream; i is taken modulo the section sum."""
+    sd = sum(sections)
+    sec = i % sd if sd > 0 else i
+    if sec % 3 == 1 and sec < 3 * sections[1]:
+        return 1
+    if sec % 3 == 2 and sec < 3 * sections[2]:
+        return 2
+    if sec % 3 == 0 and sec < 3 * sections[0]:
+        return 0
+    return 3
+
+
+def rope(x, pos, mode: int, n_dims: int, freq_base: float, sections=(0, 0, 0, 0)) -> np.ndarray:
+    """Rotary embedding of x [T, H, HD] in float64, NEOX pairing (i, i + n_dims/2) as ggml_rope_ext with
+    GGML_ROPE_TYPE_NEOX (the reference's numpy form: rope_llm, scripts/parity_minicpmo_seg.py:368-378)
+    and ggml_rope_multi with IMROPE.  theta = p * freq_base^(-2i/n_dims) exactly (ggml accumulates it
+    by repeated f32 multiplication).  pos: [T] (NEOX) or [4, T] (IMROPE)."""
+    x = np.array(x, np.float64)
+    if mode == ROPE_NONE:
+        return x
+    T = x.shape[0]
+    half = n_dims // 2
+    i = np.arange(half)
+    inv = float(freq_base) ** (-2.0 * i / n_dims)
+    pos = np.asarray(pos, np.float64)
+    if mode == ROPE_IMROPE:
+        axis = np.array([imrope_axis(int(k), sections) for k in i])
+        p = pos.reshape(4, T)[axis, :].T                 # [T, half]
+    else:
+        p = np.repeat(pos.reshape(T, 1), half, axis=1)
+    th = p * inv[None, :]
+    c, s = np.cos(th)[:, None, :], np.sin(th)[:, None, :]
+    a, b = x[..., :half].copy(), x[..., half:n_dims].copy()
+    x[..., :half] = a * c - b * s
+    x[..., half:n_dims] = a * s + b * c
+    return x
+
+
+def qk_norm_rope(q, k, q_norm, k_norm, eps, pos, mode, n_dims, freq_base, sections=(0, 0, 0, 0)):
+    """The chain of qwen3vl_model.cpp:636-650 on one chunk: per-head RMSNorm * weight, then rope."""
+    qn = rms_norm(q, q_norm, eps) if q_norm is not None else np.asarray(q, np.float64)
+    kn = rms_norm(k, k_norm, eps) if k_norm is not None else np.asarray(k, np.float64)
+    return (rope(qn, pos, mode, n_dims, freq_base, sections), rope(kn, pos, mode, n_dims, freq_base, sections))
+
+
 # ----------------------------------------------------------------- session logic
 def can_splice(cached_ids, n_past: int, ids) -> bool:
     c = np.ascontiguousarray(cached_ids, dtype=np.int32)

@@ -65,6 +65,14 @@ class _Seg(ctypes.Structure):
     _fields_ = [("src", ctypes.c_int32), ("n_rows", ctypes.c_int32), ("keep", ctypes.c_int32)]
 
 
+class _Rope(ctypes.Structure):
+    _fields_ = [("mode", ctypes.c_int), ("n_dims", ctypes.c_int), ("freq_base", ctypes.c_float),
+                ("sections", ctypes.c_int * 4)]
+
+
+ROPE_NONE, ROPE_NEOX, ROPE_IMROPE = 0, 2, 40
+
+
 class _FaParams(ctypes.Structure):
     _fields_ = [
         ("q", ctypes.c_void_p), ("q_type", ctypes.c_int), ("q_ne", ctypes.c_int64 * 3), ("q_nb", ctypes.c_size_t * 3),
@@ -113,6 +121,7 @@ def lib() -> ctypes.CDLL:
         "sv_session_begin_turn": (I, [P, I, ctypes.POINTER(I), ctypes.POINTER(I), P]),
         "sv_session_end_turn": (I, [P, I, I, I]),
         "sv_session_rows": (I, [P, ctypes.POINTER(I), P, I]),
+        "sv_qk_norm_rope_append": (I, [P, I, P, P, P, I, I, P, P, ctypes.c_float, P, P, I, P, P, I, P]),
         "sv_session_make_room": (I, [P, I, I, ctypes.POINTER(I), ctypes.POINTER(ctypes.c_int64), P]),
         "sv_session_push_rows": (I, [P, I]),
         "sv_selftest_wait_timeout": (I, [P, P, ctypes.c_uint, P]),
@@ -276,6 +285,26 @@ class KvCache:
         qt = TYPE_F32 if q.dtype == torch.float32 else TYPE_F16
         _check("sv_attn", lib().sv_attn(self.h, layer, _ptr(q), qt, T, NH, n_past, scale, _ptr(out), _stream(stream)))
         return out
+
+    def norm_rope_append(self, layer: int, q, k, v, pos, rope=None, q_norm=None, k_norm=None, eps: float = 1e-6,
+                         base: int = 0, base_dev=None, q_out=None, stream=None):
+        """q/k RMSNorm + rotary embedding + K/V append (sv_qk_norm_rope_append).  q [T, NH, HD],
+        k/v [T, NKV, HD] f32; pos int32 [T] (NEOX) or [4, T] (IMROPE); rope = (mode, n_dims,
+        freq_base, sections) or None.  Returns the rotated queries (f16 unless q_out is given)."""
+        import torch
+        T, NH, HD = q.shape
+        if q_out is None:
+            q_out = torch.empty((T, NH, HD), dtype=torch.float16, device=q.device)
+        qt = TYPE_F32 if q_out.dtype == torch.float32 else TYPE_F16
+        rp = None
+        if rope is not None:
+            mode, n_dims, freq_base, sections = rope
+            rp = _Rope(mode, n_dims, freq_base, (ctypes.c_int * 4)(*sections))
+        _check("sv_qk_norm_rope_append",
+               lib().sv_qk_norm_rope_append(self.h, layer, _ptr(q), _ptr(k), _ptr(v), T, NH, _ptr(q_norm), _ptr(k_norm),
+                                            eps, ctypes.byref(rp) if rp is not None else None, _ptr(pos), base,
+                                            _ptr(base_dev), _ptr(q_out), qt, _stream(stream)))
+        return q_out
 
     def attn_window(self, layer: int, q, lo, hi, own, max_span: int, scale: float, out=None, stream=None):
         """Per-query window attention (multi-session batch): q [n_q, n_head, head_dim]."""

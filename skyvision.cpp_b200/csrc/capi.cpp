@@ -746,6 +746,58 @@ int sv_attn_append_at_peer(sv_kv* kv, int layer, const void* q, int q_type, cons
                          static_cast<cudaStream_t>(stream), /*allow_cluster=*/true);
 }
 
+int sv_qk_norm_rope_append(sv_kv* kv, int layer, const float* q, const float* k, const float* v, int T, int n_head,
+                           const float* q_norm, const float* k_norm, float eps, const sv_rope* rope,
+                           const int32_t* pos, int slot_base, const int32_t* slot_base_dev, void* q_out,
+                           int q_out_type, void* stream) {
+    if (!kv || layer < 0 || layer >= kv->n_layer || !q || !k || !v || T <= 0 || n_head <= 0 || !q_out ||
+        !(eps >= 0.0f))
+        return SV_ERR_INVALID;
+    if (n_head % kv->n_kv_head != 0) return SV_ERR_UNSUPPORTED;
+    if (q_out_type != SV_TYPE_F16 && q_out_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    const int mode = rope ? rope->mode : SV_ROPE_NONE;
+    if (mode != SV_ROPE_NONE) {
+        if (!pos || !(rope->freq_base > 0.0f)) return SV_ERR_INVALID;
+        if (mode == SV_ROPE_IMROPE)
+            for (int i = 0; i < 4; i++)
+                if (rope->sections[i] < 0) return SV_ERR_INVALID;
+    }
+    if (!rope_supported(kv->head_dim, mode, mode == SV_ROPE_NONE ? kv->head_dim : rope->n_dims))
+        return SV_ERR_UNSUPPORTED;
+    if (!slot_base_dev && (slot_base < 0 || (int64_t)slot_base + T > kv->n_ctx)) return SV_ERR_OVERFLOW;
+    DeviceGuard g(kv->device);
+    RopeLaunch r{};
+    r.q = q;
+    r.k = k;
+    r.v = v;
+    r.T = T;
+    r.NH = n_head;
+    r.NKV = kv->n_kv_head;
+    r.HD = kv->head_dim;
+    r.qn = q_norm;
+    r.kn = k_norm;
+    r.eps = eps;
+    r.mode = mode;
+    r.n_dims = mode == SV_ROPE_NONE ? kv->head_dim : rope->n_dims;
+    r.freq_base = mode == SV_ROPE_NONE ? 1.0f : rope->freq_base;
+    for (int i = 0; i < 4; i++) r.sec[i] = mode == SV_ROPE_IMROPE ? rope->sections[i] : 0;
+    r.pos = pos;
+    r.slot_base = slot_base;
+    r.slot_base_dev = slot_base_dev;
+    r.kc = kv->tensor(layer, 0);
+    r.vc = kv->tensor(layer, 1);
+    r.row_bytes = kv->row_bytes;
+    r.kv_type = kv->type;
+    r.n_ctx = kv->n_ctx;
+    r.q_out = q_out;
+    r.q_out_type = q_out_type;
+    r.err = kv->err;
+    // the kernel lets the next launch start early, so that launch must not read cache rows before
+    // its grid dependency resolves
+    kv->rows_written_last = true;
+    return cuda_status(launch_qk_norm_rope_append(r, static_cast<cudaStream_t>(stream)));
+}
+
 int sv_soft_max_ext(const float* x, int64_t ne0, int64_t n_rows, size_t x_nb1, const void* mask, int64_t mask_rows,
                     size_t mask_nb1, float scale, float* y, size_t y_nb1, void* stream) {
     if (!x || !y || ne0 <= 0 || n_rows < 0 || (mask && mask_rows <= 0)) return SV_ERR_INVALID;

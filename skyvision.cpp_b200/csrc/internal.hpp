@@ -161,6 +161,33 @@ cudaError_t launch_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_ro
 
 cudaError_t launch_counter_add(int32_t* counter, int n, int delta, cudaStream_t st);
 
+// q/k RMSNorm + rotary embedding + K/V append (rope.cu)
+struct RopeLaunch {
+    const float* q;
+    const float* k;
+    const float* v;
+    int T, NH, NKV, HD;
+    const float* qn;
+    const float* kn;
+    float eps;
+    int mode, n_dims;
+    float freq_base;
+    int sec[4];
+    const int32_t* pos;
+    int slot_base;
+    const int32_t* slot_base_dev;
+    uint8_t* kc;
+    uint8_t* vc;
+    size_t row_bytes;
+    int kv_type;
+    int n_ctx;
+    void* q_out;
+    int q_out_type;
+    int* err;
+};
+bool rope_supported(int head_dim, int mode, int n_dims);
+cudaError_t launch_qk_norm_rope_append(const RopeLaunch& r, cudaStream_t st);
+
 cudaError_t launch_compact(KvHandle* kv, const int32_t* seg_dev_unused, const sv_segment* segs, int n_segs,
                            int dst_base, cudaStream_t st);
 

@@ -21,6 +21,9 @@ What pins what:
   parity_minicpmo_seg.py:308-365 (prefill 6 + two decode steps).
   Inputs are drawn with the reference seg-test generator (src/core/test/
   seg_test.hpp:57-68, uniform [-1, 1]), restated below.
+* q/k RMSNorm * weight then NEOX rotary embedding -> the reference's numpy
+  ``rms_norm`` and ``rope_llm`` (scripts/parity_minicpmo_seg.py:29-30,
+  368-378), theta 1e6, positions 0.. and 8190..
 
 Usage:  python tests/golden/make_golden.py [--reference /root/reference]
 """
@@ -213,6 +216,20 @@ def main() -> None:
     g["geo_v"] = vc.view(np.uint16)
     g["geo_out"] = o
     g["geo_base"] = np.array(base)
+
+    # ------------------------------------------- q/k RMSNorm + NEOX rope: the reference's numpy forms
+    # rms_norm (parity_minicpmo_seg.py:29-30) and rope_llm (:368-378), theta = 1e6, at small and large
+    # positions (chunk 0 and a chunk past 8k tokens)
+    r = SegRng(0x0B200002)
+    for tag, T, H, HD, p0 in (("a", 5, 3, 64, 0), ("b", 4, 2, 128, 8190)):
+        x = r.rnd(T * H * HD, 3.0).reshape(T, H, HD)
+        w = 1.0 + r.rnd(HD, 0.5)
+        pos = np.arange(p0, p0 + T)
+        y = cpmo.rope_llm(cpmo.rms_norm(x.astype(np.float64), w.astype(np.float64), 1e-6), pos, HD, 1e6)
+        g[f"rope_{tag}_x"] = x
+        g[f"rope_{tag}_w"] = w
+        g[f"rope_{tag}_pos"] = pos.astype(np.int32)
+        g[f"rope_{tag}_out"] = y
 
     np.savez_compressed(args.out, **g)
     print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")

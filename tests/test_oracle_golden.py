@@ -89,3 +89,13 @@ def test_attn_baseline_geometry(golden, orc):
     S = k.shape[0]
     out = orc.attn(q, _cache(k), _cache(v), orc.TYPE_F16, 8, 128, S, 1 / np.sqrt(128), orc.MASK_CAUSAL, base)
     _check(out, golden["geo_out"])
+
+
+def test_qk_norm_rope_neox_matches_reference(golden, orc):
+    """The oracle's RMSNorm * weight + NEOX rope against the reference's numpy forms
+    (scripts/parity_minicpmo_seg.py rms_norm and rope_llm), small and large positions."""
+    for tag in ("a", "b"):
+        x, w, pos = golden[f"rope_{tag}_x"], golden[f"rope_{tag}_w"], golden[f"rope_{tag}_pos"]
+        HD = x.shape[-1]
+        got = orc.rope(orc.rms_norm(x, w, 1e-6), pos, orc.ROPE_NEOX, HD, 1e6)
+        np.testing.assert_allclose(got, golden[f"rope_{tag}_out"], rtol=1e-12, atol=1e-12)
