@@ -55,7 +55,7 @@ def parse():
     ap.add_argument("--no-batched", action="store_true", help="skip the config-5 multi-session leg")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="longctx: how each layer's head outputs reach every rank")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx", "kernels"],
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx", "kernels", "outproj"],
                     help="cfg2: the headline line; longctx: one 131072-token session sharded by kv head; "
                          "kernels: one small launch set of every kernel (for ncu captures)")
     return ap.parse_args()
@@ -1022,6 +1022,88 @@ def run_longctx(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_outproj(args, world, rank, local):
+    """The step after a head-sharded session's attention: the output projection of this rank's heads
+    with the sum over ranks fused in (sv_out_proj_peer), Qwen3-VL-4B geometry (K = 32 x 128 = 4096
+    attention inputs, D = 2560 outputs, f16 weights), one decode token through 36 layers per step in
+    one CUDA graph.  Strong scaling: each rank reads its K/G columns of every layer's weights
+    (D x K/G x 2 bytes) and the ranks exchange [1, D] f32 partials over NVLink."""
+    import torch
+    import torch.distributed as dist
+    from __graft_entry__ import load_package
+    sv = load_package()
+    dev = torch.device(f"cuda:{local}")
+    stream = torch.cuda.Stream(device=dev)
+    K, W = args.steps, args.warmup
+    Ktot, D = NH * HD, 2560
+    kl = Ktot // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6000 + rank)
+    w = (torch.randn(L, D, Ktot, generator=gen, device=dev) * 0.02).half()
+    x = torch.randn(L, 1, kl, generator=gen, device=dev).half()
+    out = torch.empty(L, 1, D, dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    peer = sv.Peer(local, rank, world, L, world * D * 4)
+    mine = peer.export()
+    handles = [None] * world
+    if world > 1:
+        dist.all_gather_object(handles, mine)
+    else:
+        handles = [mine]
+    peer.import_handles(handles)
+    epoch = torch.ones(1, dtype=torch.int32, device=dev)
+    barrier(world)
+
+    def step():
+        for layer in range(L):
+            peer.out_proj(x[layer], w[layer], rank * kl, layer, epoch, out=out[layer], err=err, stream=stream)
+        sv.counter_add(epoch, 1, stream=stream)
+
+    with torch.cuda.stream(stream):
+        step()
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step()
+        for _ in range(W):
+            g.replay()
+        stream.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clk:
+            e0.record(stream)
+            for _ in range(K):
+                g.replay()
+            e1.record(stream)
+            e1.synchronize()
+        barrier(world)
+        ms = e0.elapsed_time(e1)
+    assert int(err.item()) == 0, "device wait timed out"
+    ms_max = max_over_ranks(ms, world)
+    del g
+    barrier(world)
+    peer.free()
+    if rank != 0:
+        return
+    hbm, _, _ = measured_peaks()
+    wbytes = L * D * kl * 2
+    line = {
+        "metric": "output projection tokens/s, head-sharded with the sum over ranks fused in",
+        "value": K / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16", "data": "synthetic",
+        "config": {"workload": f"36 layers x (1 x {Ktot // world}) @ ({Ktot // world} x {D}) f16 per rank, partials "
+                               "summed over ranks through NVLink peer memory in the same kernel",
+                   "parallelism": f"head (column) sharding over {world} GPU(s)"},
+        "us_per_layer": ms_max / K / L * 1e3,
+        "weight_gbs_per_gpu": wbytes / (ms_max / K * 1e-3) / 1e9,
+        "hbm_frac_per_gpu": wbytes / (ms_max / K * 1e-3) / 1e9 / hbm,
+        "gpu_launches": K * (L + 1),
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world, rank, local = (1, 0, 0)
@@ -1037,6 +1119,8 @@ def main():
     try:
         if args.workload == "longctx":
             run_longctx(args, world, rank, local)
+        elif args.workload == "outproj":
+            run_outproj(args, world, rank, local)
         else:
             run_svkv(args, world, rank, local)
     finally:

@@ -351,6 +351,24 @@ int sv_peer_import(sv_peer* p, const void* handles);
 int sv_peer_slot(const sv_peer* p, int slot, void** data);
 int sv_peer_wait(sv_peer* p, int slot, const int32_t* epoch_dev, int per_epoch, int* err_dev, void* stream);
 int sv_peer_destroy(sv_peer* p);
+
+/* The step after attention, head-sharded (qwen3vl_model.cpp:664-667, attn = mul_mat(L.o, attn)):
+ * rank g multiplies its heads' attention rows x (T rows of K_local elements, f16 or f32, row
+ * stride x_nb_t bytes) by its column slice [k_offset, k_offset + K_local) of the f16 projection
+ * w (D rows of K_total, 16-byte aligned), and the ranks' partials are summed into out (f32
+ * [T][D]) on every rank, in rank order, so every rank gets the same bits.  One kernel: the
+ * partials go into every rank's slot `slot` over peer memory and are counted on every rank's
+ * counter; each rank waits (bounded, on the device; err_dev, may be NULL, gets
+ * SV_DEVERR_TIMEOUT) for the current epoch's partials of all ranks, then sums.  Every rank calls
+ * it with the same D, T and slot; slot_bytes >= world * T * D * 4.  Like the attention gather,
+ * each slot is used once per epoch (one slot per layer; *epoch_dev counts steps from 1 and the
+ * caller advances it after each step), so consecutive calls use different slots.  T <= 8,
+ * K_local <= 4096 and multiples of 8.  No reference counterpart (the
+ * reference runs one process per model); replaces an NCCL all-gather of the attention rows
+ * followed by the full projection on every rank. */
+int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, const void* w, int K_total, int k_offset,
+                     int K_local, int D, int T, int slot, const int32_t* epoch_dev, float* out, int* err_dev,
+                     void* stream);
 int sv_attn_append_at_peer(sv_kv* kv, int layer, const void* q, int q_type, const void* k_new, const void* v_new,
                            int T, int n_head, const int32_t* n_past_dev, int max_keys, float scale, sv_peer* peer,
                            int head_offset, int n_head_total, int slot, int wait_slot, const int32_t* epoch_dev,

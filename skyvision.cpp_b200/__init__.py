@@ -130,6 +130,7 @@ def lib() -> ctypes.CDLL:
         "sv_peer_import": (I, [P, P]),
         "sv_peer_slot": (I, [P, I, ctypes.POINTER(P)]),
         "sv_peer_wait": (I, [P, I, P, I, P, P]),
+        "sv_out_proj_peer": (I, [P, P, I, ctypes.c_int64, P, I, I, I, I, I, I, P, P, P, P]),
         "sv_peer_destroy": (I, [P]),
         "sv_attn_append_at_peer": (I, [P, I, P, I, P, P, I, I, P, I, F, P, I, I, I, I, P, P]),
     }
@@ -365,6 +366,20 @@ class Peer:
         _check("sv_peer_slot", lib().sv_peer_slot(self.h, s, ctypes.byref(p)))
         t = device_view(p.value, self.slot_bytes, self.device).view(torch.float32)
         return t if shape is None else t[: int(np.prod(shape))].view(*shape)
+
+    def out_proj(self, x, w, k_offset: int, slot: int, epoch_dev, out=None, err=None, stream=None):
+        """This rank's output-projection partial x [T, K_local] (f16/f32) @ w[:, k_offset:k_offset+K_local]^T
+        (w f16 [D, K_total]), summed over every rank through peer memory (sv_out_proj_peer) -> [T, D] f32."""
+        import torch
+        T, KL = x.shape
+        D, KT = w.shape
+        if out is None:
+            out = torch.empty((T, D), dtype=torch.float32, device=x.device)
+        xt = TYPE_F32 if x.dtype == torch.float32 else TYPE_F16
+        _check("sv_out_proj_peer", lib().sv_out_proj_peer(self.h, _ptr(x), xt, x.stride(0) * x.element_size(), _ptr(w),
+                                                          KT, k_offset, KL, D, T, slot, _ptr(epoch_dev), _ptr(out),
+                                                          _ptr(err), _stream(stream)))
+        return out
 
     def wait(self, s: int, epoch_dev, per_epoch: int, err=None, stream=None) -> None:
         _check("sv_peer_wait", lib().sv_peer_wait(self.h, s, _ptr(epoch_dev), per_epoch, _ptr(err), _stream(stream)))

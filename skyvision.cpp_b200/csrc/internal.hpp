@@ -186,6 +186,25 @@ struct RopeLaunch {
     int* err;
 };
 bool rope_supported(int head_dim, int mode, int n_dims);
+
+// output projection of this rank's heads + sum over ranks through peer memory (out_proj.cu)
+struct OutProjLaunch {
+    const void* x;
+    int x_type;
+    int64_t x_nb_t;
+    const uint16_t* w;
+    int K_total, k_offset, K_local, D, T;
+    float* const* peer_out;
+    unsigned int* const* peer_ctr;
+    int n_peers, rank;
+    const unsigned int* my_ctr;
+    const float* my_slot;
+    const int32_t* epoch_dev;
+    float* out;
+    int* err;
+};
+cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st);
+int out_proj_max_t();
 cudaError_t launch_qk_norm_rope_append(const RopeLaunch& r, cudaStream_t st);
 
 cudaError_t launch_compact(KvHandle* kv, const int32_t* seg_dev_unused, const sv_segment* segs, int n_segs,

@@ -148,6 +148,47 @@ int sv_peer_wait(sv_peer* p, int slot, const int32_t* epoch_dev, int per_epoch, 
     return e == cudaSuccess ? SV_OK : SV_ERR_CUDA;
 }
 
+int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, const void* w, int K_total, int k_offset,
+                     int K_local, int D, int T, int slot, const int32_t* epoch_dev, float* out, int* err_dev,
+                     void* stream) {
+    if (!p || !p->imported || !x || !w || !out || !epoch_dev || slot < 0 || slot >= p->n_slots || T <= 0 || D <= 0 ||
+        K_local <= 0 || k_offset < 0 || (int64_t)k_offset + K_local > K_total)
+        return SV_ERR_INVALID;
+    if (x_type != SV_TYPE_F16 && x_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
+    // 16-byte weight loads: row starts and the column slice on 8-element boundaries; x staged in
+    // shared memory (T x K_local f32 <= 128 KB)
+    if (T > svkv::out_proj_max_t() || (K_total & 7) || (k_offset & 7) || (K_local & 7) || K_local > 4096 ||
+        (reinterpret_cast<uintptr_t>(w) & 15))
+        return SV_ERR_UNSUPPORTED;
+    if ((size_t)p->world * T * D * sizeof(float) > p->slot_bytes) return SV_ERR_INVALID;
+    if (x_nb_t < (int64_t)K_local * (x_type == SV_TYPE_F32 ? 4 : 2)) return SV_ERR_INVALID;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(p->device);
+    svkv::OutProjLaunch r{};
+    r.x = x;
+    r.x_type = x_type;
+    r.x_nb_t = x_nb_t;
+    r.w = static_cast<const uint16_t*>(w);
+    r.K_total = K_total;
+    r.k_offset = k_offset;
+    r.K_local = K_local;
+    r.D = D;
+    r.T = T;
+    r.peer_out = p->d_out + (size_t)slot * p->world;
+    r.peer_ctr = p->d_ctr + (size_t)slot * p->world;
+    r.n_peers = p->world;
+    r.rank = p->rank;
+    r.my_ctr = p->ctr(slot);
+    r.my_slot = reinterpret_cast<const float*>(p->buf + (size_t)slot * p->slot_bytes);
+    r.epoch_dev = epoch_dev;
+    r.out = out;
+    r.err = err_dev;
+    const cudaError_t e = svkv::launch_out_proj_peer(r, static_cast<cudaStream_t>(stream));
+    cudaSetDevice(prev);
+    return e == cudaSuccess ? SV_OK : SV_ERR_CUDA;
+}
+
 int sv_peer_destroy(sv_peer* p) {
     if (!p) return SV_OK;
     int prev = 0;
