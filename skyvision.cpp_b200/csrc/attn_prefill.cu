@@ -3,7 +3,10 @@
 //
 // Replaces ggml_flash_attn_ext for prompt chunks (the 512-token ubatches of
 // gemma4_model.cpp:1355-1395, the splice tail of qwen3vl_model.cpp:1172-1193)
-// over an f16 cache, causal mask as an in-kernel predicate
+// over an f16 cache, or a q8_0 cache whose visible rows q8_0_split_kernel (end of
+// this file) rewrote as f16 (hi, lo) planes: K and V tiles then enter the MMA as two
+// parts each (NP = 2) and P as two parts (PL = 2), so the q8_0 values and the
+// weights keep ~22 bits.  Causal mask as an in-kernel predicate
 // (set_causal_mask(mask, n_past, T), attention.hpp:60-67).
 //
 // Work unit: NQT query tiles of 128 rows (NQT = 2 at HD 128 when the chunk has two) x one kv
@@ -36,10 +39,11 @@
 // handle's workspace, and the last waits (bounded) for them and merges with its own partial,
 // which never leaves TMEM.
 //
-// Measured (config 2 splice tail, 384 over 4096 cached rows, one B200): 432 TFLOP/s over 36
-// layers.  In-kernel timestamps put the limiter in the softmax warps' per-tile chain (TMEM load,
-// row max, exponentials, P store: ~1500 cycles per 64-key tile) rather than in the tensor pipe
-// (~550 cycles of MMA per tile pair) or in L2.
+// Measured (config 2 splice tail, 384 over 4096 cached rows, one B200): 448 TFLOP/s over 36
+// layers; config 4's q8_0 chunks 280 TFLOP/s (algorithmic).  In-kernel clock stamps per 64-key
+// tile (two query tiles): ~3250 cycles a tile, of which the softmax warps compute ~2000 and wait
+// ~1160 for the next S, while the issuing thread blocks ~1340 cycles issuing the tile's 16 N = 64
+// S MMAs.
 //
 // Roofline: tensor-bound.  Algorithmic FLOPs per launch = 4 * NH * HD * sum
 // over queries of visible keys (masked keys do not count).
