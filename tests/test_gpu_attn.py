@@ -256,6 +256,28 @@ def test_flash_attn_ext_explicit_mask(orc):
     close(out.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("T", [40, 1])
+def test_flash_attn_ext_q8_0_views(orc, T):
+    """ggml_flash_attn_ext over q8_0 cache views (config 4 geometry: 16q/4kv HD 256, K/V with 1%
+    outliers x8), f32 queries and an explicit set_causal_mask-style f16 mask: a 40-token chunk and
+    one decode token through the view entry point (no cache handle)."""
+    NKV, HD, NH, S = 4, 256, 16, 900
+    base = S - T
+    ne0 = NKV * HD
+    k = orc.q8_0_quantize(orc.f16_to_f32(orc.normal_f16(14, 1, S * ne0, outlier_frac=0.01).reshape(S, ne0)))
+    v = orc.q8_0_quantize(orc.f16_to_f32(orc.normal_f16(14, 2, S * ne0, outlier_frac=0.01).reshape(S, ne0)))
+    q16 = orc.normal_f16(14, 3 + T, T * NH * HD).reshape(T, NH, HD)
+    q = orc.f16_to_f32(q16)
+    mask = np.zeros((T, S), np.float32)
+    for t in range(T):
+        mask[t, base + t + 1:] = -np.inf
+    m16 = mask.astype(np.float16)
+    out = sv.flash_attn_ext(torch.from_numpy(q).to(DEV), torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV),
+                            torch.from_numpy(m16).to(DEV), 1 / 16.0, NKV, HD, S, kv_type=sv.TYPE_Q8_0)
+    ref = orc.attn(q, k, v, orc.TYPE_Q8_0, NKV, HD, S, 1 / 16.0, orc.MASK_EXPLICIT, mask=m16.view(np.uint16))
+    close(out.cpu().numpy(), ref)
+
+
 def test_fully_masked_row_is_zero(orc):
     NKV, HD, NH, S = 2, 64, 8, 70
     k = orc.normal_f16(5, 1, S * NKV * HD).reshape(S, -1)

@@ -101,3 +101,29 @@ def test_out_proj_two_ranks():
         assert flags == 0
         assert err <= 1e-5
     assert res[0][2] == res[1][2]          # every rank sums in rank order: identical bits
+
+
+def test_out_proj_wait_expires_and_reports():
+    """The cross-rank wait is bounded: with the epoch set one step ahead nothing can reach the target
+    count (a flag nothing sets), so every CTA gives up after the 2 s limit, the timeout bit reaches
+    the host, and the context stays usable (a fresh peer group then computes the right product)."""
+    sv = load_package()
+    dev = torch.device("cuda:0")
+    x, w = _data(1)
+    xd = torch.from_numpy(x[0]).to(dev)
+    wd = torch.from_numpy(w).to(dev)
+    peer = sv.Peer(0, 0, 1, 1, D * 4)
+    peer.import_handles([peer.export()])
+    epoch = torch.full((1,), 2, dtype=torch.int32, device=dev)      # the first call is epoch 1
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    peer.out_proj(xd, wd, 0, 0, epoch, err=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & sv.DEVERR_TIMEOUT
+    peer.free()
+    fresh = sv.Peer(0, 0, 1, 1, D * 4)
+    fresh.import_handles([fresh.export()])
+    epoch.fill_(1)
+    out = fresh.out_proj(xd, wd, 0, 0, epoch).cpu().numpy()
+    ref = x[0].astype(np.float64) @ w.astype(np.float64).T
+    assert np.abs(out - ref).max() <= 1e-5 * np.abs(ref).max()
+    fresh.free()
