@@ -814,8 +814,9 @@ def run_kernels(args):
     fused decode (config 2 geometry, S = 4481), windowed decode (2 sessions of ~19k rows),
     chunked prefill (384 over 4096), f16 and q8_0 append, compaction, fused q8_0 decode and the last q8_0
     prefill chunk (config 4 geometry: q8_0_split_kernel, then the tensor-core kernel on hi + lo parts), and
-    the fused q/k norm + IMROPE + append of a config 2 splice tail (384 tokens).  Under 1 GB on the
-    device; used by the committed ncu summaries."""
+    the fused q/k norm + IMROPE + append of a config 2 splice tail (384 tokens), and the sharded output
+    projection on one rank (K 4096, D 2560).  Under 1 GB on the device; used by the committed ncu
+    summaries."""
     import torch
     from __graft_entry__ import load_package
     sv = load_package()
@@ -877,6 +878,16 @@ def run_kernels(args):
     wr = torch.ones(HD, device=dev)
     timed("norm_rope_append_us", lambda: kv.norm_rope_append(0, qr, kr, kr, pr, rope=(sv.ROPE_IMROPE, HD, 5e6, (24, 20, 20, 0)),
                                                              q_norm=wr, k_norm=wr, base=PRE))
+    # the sharded output projection on one rank (its own slot; one slot per call, each its own epoch)
+    peer = sv.Peer(0, 0, 1, 3, 2560 * 4)
+    peer.import_handles([peer.export()])
+    wo = (torch.randn(2560, NH * HD, generator=g, device=dev) * 0.02).half()
+    xo = torch.randn(1, NH * HD, generator=g, device=dev).half()
+    ep = torch.ones(1, dtype=torch.int32, device=dev)
+    calls = iter(range(3))
+    timed("out_proj_us", lambda: peer.out_proj(xo, wo, 0, next(calls), ep))
+    torch.cuda.synchronize()
+    peer.free()
     torch.cuda.synchronize()
     assert kv.error_flags() == 0 and kq.error_flags() == 0 and kw.error_flags() == 0
     print(json.dumps({"workload": "kernels", "us_per_launch": times}), flush=True)
