@@ -810,6 +810,7 @@ int sv_soft_max_ext(const float* x, int64_t ne0, int64_t n_rows, size_t x_nb1, c
 int sv_kv_compact(sv_kv* kv, const sv_segment* segs, int n_segs, int dst_base, int* new_len, void* stream) {
     if (!kv || (!segs && n_segs > 0) || n_segs < 0 || dst_base < 0) return SV_ERR_INVALID;
     if (n_segs > 1024) return SV_ERR_UNSUPPORTED;
+    if (kv->row_bytes % 16 != 0) return SV_ERR_UNSUPPORTED;   // rows move as 16-byte vectors
     int64_t kept = 0;
     int64_t prev_end = -1;
     for (int s = 0; s < n_segs; s++) {

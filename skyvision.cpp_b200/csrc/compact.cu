@@ -28,6 +28,7 @@ namespace {
 constexpr int kMaxSegs = 1024;
 constexpr int kCompactThreads = 256;
 constexpr int kRowsPerCta = 8;
+constexpr int kCopyUnroll = 4;
 constexpr int kMaxWaves = 16;
 
 struct CompactParams {
@@ -84,31 +85,57 @@ __global__ void __launch_bounds__(kCompactThreads) compact_kernel(const __grid_c
     uint8_t* dst_t = p.dst_base_ptr + (size_t)z * p.dst_tstride;
     const int j0 = p.j_lo + blockIdx.x * kRowsPerCta;
     const int vec_per_row = (int)(p.row_bytes / 16);
-    for (int rr = 0; rr < kRowsPerCta; rr++) {
-        const int j = j0 + rr;
-        if (j >= p.j_hi) break;
-        int64_t src_row;
-        if (p.src_from_segments) {
-            // last segment whose kept offset <= j among kept segments
-            int lo = 0, hi = p.n_segs - 1;
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (kept_off[mid] <= j) lo = mid; else hi = mid - 1;
+    // the CTA's rows first (one thread per row), then every thread moves kCopyUnroll vectors with all
+    // of its loads issued before its stores: rows one after another left one memory round trip per
+    // row and half the threads idle on 2 KB rows.  Rows of one wave never overlap (see above), so
+    // the order inside a launch is free.
+    __shared__ int64_t srow[kRowsPerCta], drow[kRowsPerCta];
+    if (tid < kRowsPerCta) {
+        const int j = j0 + tid;
+        int64_t src_row = -1, dst_row = -1;
+        if (j < p.j_hi) {
+            if (p.src_from_segments) {
+                // last segment whose kept offset <= j among kept segments
+                int lo = 0, hi = p.n_segs - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (kept_off[mid] <= j) lo = mid; else hi = mid - 1;
+                }
+                // skip zero-length / dropped segments that share the same offset
+                while (lo < p.n_segs - 1 && !(p.segs[lo].keep && kept_off[lo] + p.segs[lo].n_rows > j)) lo++;
+                src_row = (int64_t)p.segs[lo].src + (j - kept_off[lo]);
+                if (src_row < 0 || src_row >= p.n_rows_cache) {
+                    if (p.err) atomicOr(p.err, ERRBIT_SEGMENT);
+                    src_row = -1;
+                }
+            } else {
+                src_row = j - p.j_lo;
             }
-            // skip zero-length / dropped segments that share the same offset
-            while (lo < p.n_segs - 1 && !(p.segs[lo].keep && kept_off[lo] + p.segs[lo].n_rows > j)) lo++;
-            src_row = (int64_t)p.segs[lo].src + (j - kept_off[lo]);
-            if (src_row < 0 || src_row >= p.n_rows_cache) {
-                if (tid == 0 && p.err) atomicOr(p.err, ERRBIT_SEGMENT);
-                continue;
-            }
-        } else {
-            src_row = j - p.j_lo;
+            if (src_row >= 0) dst_row = p.dst_from_base ? (int64_t)p.dst_base + j : (int64_t)(j - p.j_lo);
         }
-        const int64_t dst_row = p.dst_from_base ? (int64_t)p.dst_base + j : (int64_t)(j - p.j_lo);
-        const uint4* s4 = reinterpret_cast<const uint4*>(src_t + (size_t)src_row * p.row_bytes);
-        uint4* d4 = reinterpret_cast<uint4*>(dst_t + (size_t)dst_row * p.row_bytes);
-        for (int k = tid; k < vec_per_row; k += kCompactThreads) d4[k] = s4[k];
+        srow[tid] = src_row;
+        drow[tid] = dst_row;
+    }
+    __syncthreads();
+    const int total = kRowsPerCta * vec_per_row;
+    for (int base = tid; base < total; base += kCompactThreads * kCopyUnroll) {
+        uint4 v[kCopyUnroll];
+        int64_t dst_off[kCopyUnroll];
+#pragma unroll
+        for (int u = 0; u < kCopyUnroll; u++) {
+            const int idx = base + u * kCompactThreads;
+            dst_off[u] = -1;
+            if (idx < total) {
+                const int r = idx / vec_per_row, k = idx % vec_per_row;
+                if (srow[r] >= 0) {
+                    v[u] = reinterpret_cast<const uint4*>(src_t + (size_t)srow[r] * p.row_bytes)[k];
+                    dst_off[u] = (int64_t)drow[r] * (int64_t)p.row_bytes + (int64_t)k * 16;
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kCopyUnroll; u++)
+            if (dst_off[u] >= 0) *reinterpret_cast<uint4*>(dst_t + dst_off[u]) = v[u];
     }
 }
 
