@@ -72,8 +72,8 @@ struct GqaCfg {
     static_assert(ROWS_MAX * (HD / 4) <= kCThreads, "one (row, 4-column) group per consumer thread");
     // cluster merge, merger CTA only: partial O [split][row][HD] and (m, l) [split][row]
     static constexpr int PUSH_O = 0;
-    static constexpr int PUSH_ML = 16 * kRows * HD * 4;
-    static_assert(PUSH_ML + 16 * kRows * 8 <= RING_B, "merge slots must fit in the stage ring");
+    static constexpr int PUSH_ML = 16 * ROWS_MAX * HD * 4;
+    static_assert(PUSH_ML + 16 * ROWS_MAX * 8 <= RING_B, "merge slots must fit in the stage ring");
     static constexpr int BAR_OFF = RING_B;
     static constexpr int SMEM = BAR_OFF + (2 * STAGES + 1) * 8 + 16;   // + abort and last-split flags
     static_assert(SMEM + 1024 <= 227 * 1024, "shared memory budget");
@@ -259,7 +259,7 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
             float2 ml[16];
 #pragma unroll
             for (int sp = 0; sp < 16; sp++)
-                if (sp < ns) ml[sp] = *reinterpret_cast<const float2*>(&slot_ml[(sp * kRows + r) * 2]);
+                if (sp < ns) ml[sp] = *reinterpret_cast<const float2*>(&slot_ml[(sp * C::ROWS_MAX + r) * 2]);
             float MM = -INFINITY;
 #pragma unroll
             for (int sp = 0; sp < 16; sp++)
@@ -271,7 +271,7 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 if (sp < ns && ml[sp].x != -INFINITY) {
                     const float w = fast_exp2(ml[sp].x - MM);
                     LL += ml[sp].y * w;
-                    const float4 v = *reinterpret_cast<const float4*>(&slot_o[(sp * kRows + r) * HD + c]);
+                    const float4 v = *reinterpret_cast<const float4*>(&slot_o[(sp * C::ROWS_MAX + r) * HD + c]);
                     o4.x += v.x * w; o4.y += v.y * w; o4.z += v.z * w; o4.w += v.w * w;
                 }
             }
@@ -842,8 +842,8 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     const float* slot_o = reinterpret_cast<const float*>(smem + C::PUSH_O);
     const float* slot_ml = reinterpret_cast<const float*>(smem + C::PUSH_ML);
     const uint32_t bar = dsmem_map(smem_u32(mdata), 0);
-    st_async_f4(dsmem_map(smem_u32(&slot_o[(split * kRows + r) * HD + c]), 0), acc, bar);
-    if (c == 0) st_async_f2(dsmem_map(smem_u32(&slot_ml[(split * kRows + r) * 2]), 0), make_float2(M, L), bar);
+    st_async_f4(dsmem_map(smem_u32(&slot_o[(split * C::ROWS_MAX + r) * HD + c]), 0), acc, bar);
+    if (c == 0) st_async_f2(dsmem_map(smem_u32(&slot_ml[(split * C::ROWS_MAX + r) * 2]), 0), make_float2(M, L), bar);
 }
 
 template <int HD, int KVT, bool kPeer = false>
