@@ -24,6 +24,12 @@ What pins what:
 * q/k RMSNorm * weight then NEOX rotary embedding -> the reference's numpy
   ``rms_norm`` and ``rope_llm`` (scripts/parity_minicpmo_seg.py:29-30,
   368-378), theta 1e6, positions 0.. and 8190..
+* interleaved MRoPE (Qwen3-VL, sections 24/20/20) -> HF transformers'
+  ``Qwen3VLTextRotaryEmbedding`` + ``apply_rotary_pos_emb`` (transformers 5.5.0,
+  float32), the reference's own parity anchor for the qwen3vl text stack
+  (scripts/parity_onestreamer.py:1-30, 81).  ggml's IMROPE rule takes rotation
+  pairs 61 and 62 from the fourth (slot) stream, which HF takes from t; the
+  fixture's slot stream equals t (a text-only turn), where both agree.
 
 Usage:  python tests/golden/make_golden.py [--reference /root/reference]
 """
@@ -230,6 +236,27 @@ def main() -> None:
         g[f"rope_{tag}_w"] = w
         g[f"rope_{tag}_pos"] = pos.astype(np.int32)
         g[f"rope_{tag}_out"] = y
+
+    # ------------------------------------------- IMROPE: HF transformers' Qwen3-VL text rotary (float32)
+    from transformers.models.qwen3_vl import modeling_qwen3_vl as hfq
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+    import torch
+    cfg = Qwen3VLTextConfig(hidden_size=256, num_attention_heads=2, num_key_value_heads=1, head_dim=128,
+                            rope_parameters={"rope_type": "default", "rope_theta": 5e6,
+                                             "mrope_section": [24, 20, 20]})
+    rot = hfq.Qwen3VLTextRotaryEmbedding(cfg)
+    r = SegRng(0x0B200003)
+    T, H, HD = 6, 3, 128
+    x = r.rnd(T * H * HD, 3.0).reshape(T, H, HD).astype(np.float32)
+    t = np.arange(90, 90 + T)
+    hh = np.array([3, 0, 17, 39, 22, 8])
+    ww = np.array([5, 31, 0, 12, 39, 26])
+    xt = torch.from_numpy(x).permute(1, 0, 2)[None]                       # (1, H, T, HD)
+    cos, sin = rot(xt, torch.from_numpy(np.stack([t, hh, ww]))[:, None, :])
+    y, _ = hfq.apply_rotary_pos_emb(xt, xt, cos, sin)
+    g["imrope_hf_x"] = x
+    g["imrope_hf_pos"] = np.stack([t, hh, ww, t]).astype(np.int32)        # [t, h, w, slot]
+    g["imrope_hf_out"] = y[0].permute(1, 0, 2).numpy().astype(np.float64)
 
     np.savez_compressed(args.out, **g)
     print(f"wrote {args.out}: {len(g)} arrays, {os.path.getsize(args.out)} bytes")

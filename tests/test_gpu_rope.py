@@ -130,3 +130,19 @@ def test_rows_past_the_cache_set_the_error_bit(orc):
     kv.norm_rope_append(0, _t(q), _t(k), _t(v), None, base_dev=base_dev)   # device base: rows 64, 65 skipped
     torch.cuda.synchronize()
     assert kv.error_flags() & sv.DEVERR_ROW_RANGE
+
+
+def test_imrope_kernel_matches_hf_golden(orc, golden):
+    """The kernel's IMROPE (no norms, f32 queries out) against the committed HF transformers Qwen3-VL
+    rotary fixture (float32 reference, slot stream = t): within 5e-5 plus the kernel's 1e-5."""
+    x, pos = golden["imrope_hf_x"], golden["imrope_hf_pos"]
+    T, H, HD = x.shape
+    kv = sv.KvCache()
+    assert kv.alloc(0, 1, 1, HD, 256)
+    q32 = torch.empty((T, H, HD), dtype=torch.float32, device=DEV)
+    k = np.ascontiguousarray(x[:, :1])
+    kv.norm_rope_append(0, _t(x), _t(k), _t(k), _t(pos), rope=(orc.ROPE_IMROPE, HD, 5e6, (24, 20, 20, 0)),
+                        base=int(pos[3, 0]), q_out=q32)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(q32.cpu().numpy(), golden["imrope_hf_out"], rtol=0, atol=6e-5)
+    assert kv.error_flags() == 0

@@ -99,3 +99,16 @@ def test_qk_norm_rope_neox_matches_reference(golden, orc):
         HD = x.shape[-1]
         got = orc.rope(orc.rms_norm(x, w, 1e-6), pos, orc.ROPE_NEOX, HD, 1e6)
         np.testing.assert_allclose(got, golden[f"rope_{tag}_out"], rtol=1e-12, atol=1e-12)
+
+
+def test_imrope_matches_hf_qwen3vl(golden, orc):
+    """The oracle's interleaved MRoPE (ggml's IMROPE rule, sections 24/20/20/0, theta 5e6) against HF
+    transformers' Qwen3-VL text rotary, which the reference's qwen3vl parity script uses as its
+    reference.  The fixture's slot stream equals t, so the two rules agree on every rotation pair;
+    HF computes in float32 (angles of positions < 100, so |error| < 5e-5)."""
+    x, pos = golden["imrope_hf_x"], golden["imrope_hf_pos"]
+    got = orc.rope(x, pos, orc.ROPE_IMROPE, 128, 5e6, (24, 20, 20, 0))
+    np.testing.assert_allclose(got, golden["imrope_hf_out"], rtol=0, atol=5e-5)
+    # a misrouted stream shows: swapping h and w moves every pair i < 60 with i % 3 != 0
+    swapped = orc.rope(x, pos[[0, 2, 1, 3]], orc.ROPE_IMROPE, 128, 5e6, (24, 20, 20, 0))
+    assert np.abs(swapped - golden["imrope_hf_out"]).max() > 1e-2
