@@ -146,10 +146,6 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
     return y;
 }
 
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-    asm volatile("prefetch.L2 [%0];" ::"l"(p));
-}
-
 // asynchronous stores into another CTA's shared memory, counted on that CTA's mbarrier
 __device__ __forceinline__ void st_async_f4(uint32_t caddr, float4 v, uint32_t cbar) {
     asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"

@@ -197,7 +197,7 @@ struct OutProjLaunch {
     float* const* peer_out;
     unsigned int* const* peer_ctr;
     int n_peers, rank;
-    const unsigned int* my_ctr;
+    const unsigned int* my_ctr;        // this rank's band counters of the slot [kPeerBands]
     const float* my_slot;
     const int32_t* epoch_dev;
     float* out;
@@ -205,6 +205,7 @@ struct OutProjLaunch {
 };
 cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st);
 int out_proj_max_t();
+int out_proj_max_d();
 cudaError_t launch_qk_norm_rope_append(const RopeLaunch& r, cudaStream_t st);
 
 cudaError_t launch_compact(KvHandle* kv, const int32_t* seg_dev_unused, const sv_segment* segs, int n_segs,
@@ -222,16 +223,22 @@ namespace svkv {
 // Gathered-output buffers of a head-sharded session, one per rank, mapped into every rank over
 // CUDA IPC (peer memory over NVLink).  Local allocation: n_slots regions of slot_bytes, then one
 // 32-bit arrival counter per slot.
+// per slot, one arrival counter per output band of sv_out_proj_peer (its grid never exceeds this)
+constexpr int kPeerBands = 512;
 struct PeerGroup {
     int device = 0, rank = 0, world = 1, n_slots = 0;
-    size_t slot_bytes = 0, ctr_off = 0, buf_bytes = 0;
+    size_t slot_bytes = 0, ctr_off = 0, bctr_off = 0, buf_bytes = 0;
     uint8_t* buf = nullptr;
     uint8_t* base[8] = {nullptr};      // every rank's buffer in this process (base[rank] = buf)
     bool opened[8] = {false};
     float** d_out = nullptr;           // device [n_slots][world]: each rank's region of a slot
     unsigned int** d_ctr = nullptr;    // device [n_slots][world]: each rank's counter of a slot
+    unsigned int** d_bctr = nullptr;   // device [n_slots][world]: each rank's band counters of a slot
     bool imported = false;
     unsigned int* ctr(int slot) const { return reinterpret_cast<unsigned int*>(buf + ctr_off) + slot; }
+    unsigned int* bctr(int slot) const {
+        return reinterpret_cast<unsigned int*>(buf + bctr_off) + (size_t)slot * kPeerBands;
+    }
 };
 cudaError_t launch_peer_wait(const unsigned int* ctr, const int32_t* epoch_dev, unsigned int per_epoch, int* err,
                              cudaStream_t st);

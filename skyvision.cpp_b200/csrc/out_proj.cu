@@ -6,18 +6,23 @@
 // [k_offset, k_offset + K_local) of the projection's input; the full output is the sum over ranks
 // of x_g * W[:, k_offset : k_offset + K_local]^T (the row-parallel split of the projection).
 //
-// One kernel per rank and layer (every rank calls it):
-//   1. each CTA computes a band of output columns d of this rank's partial y_g[t][d] (f16 weights,
-//      f32 accumulation; one warp per column, 16-byte weight loads, x staged in shared memory), and
-//      stores them into its own region [g] of slot `slot` on every rank (plain stores to peer memory
-//      over NVLink, CUDA IPC mappings);
-//   2. after a system-scope fence it adds 1 to every rank's arrival counter of the slot;
-//   3. it waits (bounded, on the device) until its own counter holds the current epoch's arrivals of
-//      every CTA of every rank, then sums its band over the ranks in rank order, so every rank ends
-//      with bitwise the same output.
-// The grid never exceeds one CTA per SM, so every CTA of a launch is resident while any of them
-// waits, and the kernel lets the next launch start only when it exits.  A slot holds [world][T][D]
-// f32 partials; a slot is rewritten only after every rank has summed it when consecutive layers use
+// One kernel per rank and layer (every rank calls it with the same D, so CTA b covers the same band
+// of output columns on every rank):
+//   1. before the grid dependency, one thread issues the band's weight rows (this rank's column
+//      slice of each, contiguous) as untiled bulk copies into shared memory, one mbarrier per row:
+//      the weights are model constants that no kernel of the stream writes, so the whole band is in
+//      flight from the first instant and the launch is one HBM read of the weights;
+//   2. after the dependency it stages x in shared memory; each warp takes a row as soon as that
+//      row has landed, computes y_g[t][d] (f32 accumulation) and stores it into its own region [g]
+//      of slot `slot` on every rank (plain stores to peer memory over NVLink, CUDA IPC mappings);
+//   3. a system-scope release add counts the band on every rank's band counter (the CTA barrier
+//      before it orders every thread's stores), then the CTA waits (bounded, acquire loads) until its
+//      own band counter holds the current epoch's arrivals of every rank and sums the band over the
+//      ranks in rank order, so every rank ends with bitwise the same output.
+// A CTA waits only for the same band of the other ranks.  The grid never exceeds one CTA per SM,
+// so every CTA of a launch is resident while any of them waits; the next launch is let in once the
+// whole grid runs (its CTAs take SMs as these exit and issue their own weight rows meanwhile).  A slot holds [world][T][D] f32
+// partials; a slot is rewritten only after every rank has summed it when consecutive layers use
 // different slots (a rank reaches layer l + 2 only after every rank finished layer l).
 //
 // Bound: HBM on the weights (D x K_local x 2 bytes per launch) plus two NVLink latencies.
@@ -29,8 +34,11 @@ namespace svkv {
 namespace {
 
 constexpr int kOpThreads = 512;
-constexpr int kOpBatch = 16;     // 16-byte weight loads in flight per lane (a 4096-column row: all of them)
+constexpr int kOpWarps = kOpThreads / 32;
 constexpr int kOpMaxT = 8;
+constexpr int kOpMaxRows = 32;                 // weight rows staged per round (one mbarrier each)
+constexpr int kOpSmemBytes = 196 * 1024;       // x (f32) + the staged weight rows
+constexpr int kOpMaxBand = 128;                // output columns per CTA (D <= 148 x 128)
 
 struct OutProjArgs {
     const uint8_t* x;            // [T] rows of K_local elements (f16 or f32), row stride x_nb_t bytes
@@ -40,20 +48,70 @@ struct OutProjArgs {
     const uint16_t* w;           // f16 [D][K_total]
     int K_total, k_offset, K_local, D, T;
     float* const* peer_out;      // this slot's region on every rank
-    unsigned int* const* peer_ctr;
+    unsigned int* const* peer_bctr;   // this slot's band counters on every rank
     int n_peers, rank;
-    const unsigned int* my_ctr;
+    const unsigned int* my_bctr;
     const float* my_slot;        // this rank's slot: [world][T][D]
     const int32_t* epoch_dev;
     float* out;                  // [T][D] f32
     int* err;
+    int rows_per_round;          // weight rows one round stages (<= kOpMaxRows)
+    uint32_t w_off;              // byte offset of the staged weight rows in dynamic shared memory
 };
 
-__global__ void __launch_bounds__(kOpThreads) out_proj_peer_kernel(const __grid_constant__ OutProjArgs a) {
-    extern __shared__ __align__(16) float xs[];   // [T][K_local]
+__global__ void __launch_bounds__(kOpThreads, 1) out_proj_peer_kernel(const __grid_constant__ OutProjArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kOpMaxRows];
     __shared__ int ok_flag;
+    __shared__ float own[kOpMaxBand][kOpMaxT];     // this rank's partials of the band
+    __shared__ float* s_out[8];                    // the slot's region on every rank
+    __shared__ unsigned int* s_bctr[8];            // the slot's band counters on every rank
+    __shared__ unsigned int s_target;              // this epoch's arrival count of a band
+    float* xs = reinterpret_cast<float*>(smem);   // [T][K_local]
+    uint8_t* ws = smem + a.w_off;                  // [rows_per_round][K_local] f16
+    const int T = a.T, KL = a.K_local, RR = a.rows_per_round;
+    const uint32_t row_bytes = (uint32_t)KL * 2;
+    // this CTA's band of output columns
+    const int d0 = (int)((int64_t)a.D * blockIdx.x / gridDim.x);
+    const int d1 = (int)((int64_t)a.D * (blockIdx.x + 1) / gridDim.x);
+    const int nb = d1 - d0;
+    const int n_rounds = (nb + RR - 1) / RR;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < RR; i++) mbar_init(&full[i], 1);
+        fence_barrier_init();
+        ok_flag = 1;
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // warp 0 issues a round's rows, one row per lane (RR <= 32)
+    auto issue = [&](int round) {
+        const int r0 = round * RR, n = min(RR, nb - r0);
+        if (lane < n) {
+            mbar_arrive_expect_tx(&full[lane], row_bytes);
+            bulk_load_1d(ws + (size_t)lane * row_bytes, a.w + (size_t)(d0 + r0 + lane) * a.K_total + a.k_offset,
+                         row_bytes, &full[lane]);
+        }
+    };
+    if (warp == 0) issue(0);   // before the dependency: model constants only
+    if (warp == 1) {
+        // x may still be written by the previous kernel: an L2 prefetch is only a hint, so the loads
+        // after the dependency find its lines in L2 instead of queueing behind the weight stream
+        const int es = a.x_type == SV_TYPE_F32 ? 4 : 2;
+        const int lines = (KL * es + 127) / 128;
+        for (int i = lane; i < T * lines; i += 32)
+            prefetch_l2(a.x + (size_t)(i / lines) * a.x_nb_t + (size_t)(i % lines) * 128);
+    } else if (warp == 2 && lane < a.n_peers) {
+        // the slot's pointer tables (written once, when the peers were imported): read now, so no
+        // global round trip sits between the last row and the exchange
+        s_out[lane] = a.peer_out[lane];
+        s_bctr[lane] = a.peer_bctr[lane];
+    }
+    // the next launch may be scheduled now: this grid is resident (every CTA got here), and what a
+    // launch does before its dependency wait reads only model constants
+    pdl_trigger();
     pdl_wait();
-    const int T = a.T, KL = a.K_local;
+    if (threadIdx.x == 64)   // the epoch (advanced by the kernel that ends each step), read with x
+        s_target = (unsigned int)(*reinterpret_cast<const volatile int*>(a.epoch_dev)) * (unsigned int)a.n_peers;
     if (a.x_vec) {   // 8 elements per 16-byte load (K_local is a multiple of 8, so no load spans two rows)
         for (int i = threadIdx.x; i < T * KL / 8; i += blockDim.x) {
             const int e = i * 8, t = e / KL, k = e % KL;
@@ -82,35 +140,30 @@ __global__ void __launch_bounds__(kOpThreads) out_proj_peer_kernel(const __grid_
         }
     }
     __syncthreads();
-    // this CTA's band of output columns
-    const int d0 = (int)((int64_t)a.D * blockIdx.x / gridDim.x);
-    const int d1 = (int)((int64_t)a.D * (blockIdx.x + 1) / gridDim.x);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int d = d0 + warp; d < d1; d += kOpThreads / 32) {
-        const uint16_t* wr = a.w + (size_t)d * a.K_total + a.k_offset;
-        float acc[kOpMaxT];
-#pragma unroll
-        for (int t = 0; t < kOpMaxT; t++) acc[t] = 0.0f;
-        // kOpBatch weight loads per lane issued before any is used (one in flight per lane left the
-        // kernel latency-bound at ~0.4 TB/s)
-        for (int k0 = lane * 8; k0 < KL; k0 += 32 * 8 * kOpBatch) {
-            uint4 u[kOpBatch];
-#pragma unroll
-            for (int c = 0; c < kOpBatch; c++) {
-                const int k = k0 + c * 32 * 8;
-                u[c] = k < KL ? __ldg(reinterpret_cast<const uint4*>(wr + k)) : make_uint4(0, 0, 0, 0);
+    for (int round = 0; round < n_rounds; round++) {
+        if (round > 0) {
+            __syncthreads();   // every warp is done with the previous round's rows
+            if (warp == 0) issue(round);
+        }
+        const int r0 = round * RR, n = min(RR, nb - r0);
+        for (int i = warp; i < n; i += kOpWarps) {
+            if (!mbar_wait(&full[i], round & 1, a.err)) {
+                ok_flag = 0;
+                break;
             }
+            const uint8_t* wr = ws + (size_t)i * row_bytes;
+            float acc[kOpMaxT];
 #pragma unroll
-            for (int c = 0; c < kOpBatch; c++) {
-                const int k = k0 + c * 32 * 8;
-                if (k >= KL) break;
-                const __half2* h = reinterpret_cast<const __half2*>(&u[c]);
+            for (int t = 0; t < kOpMaxT; t++) acc[t] = 0.0f;
+            for (int k = lane * 8; k < KL; k += 32 * 8) {
+                const uint4 u = *reinterpret_cast<const uint4*>(wr + (size_t)k * 2);
+                const __half2* h = reinterpret_cast<const __half2*>(&u);
                 float wv[8];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float2 f = __half22float2(h[i]);
-                    wv[2 * i] = f.x;
-                    wv[2 * i + 1] = f.y;
+                for (int j = 0; j < 4; j++) {
+                    const float2 f = __half22float2(h[j]);
+                    wv[2 * j] = f.x;
+                    wv[2 * j + 1] = f.y;
                 }
 #pragma unroll
                 for (int t = 0; t < kOpMaxT; t++) {
@@ -124,48 +177,51 @@ __global__ void __launch_bounds__(kOpThreads) out_proj_peer_kernel(const __grid_
                     }
                 }
             }
-        }
+            const int d = d0 + r0 + i;
 #pragma unroll
-        for (int t = 0; t < kOpMaxT; t++) {
-            if (t < T) {
-                float s = acc[t];
+            for (int t = 0; t < kOpMaxT; t++) {
+                if (t < T) {
+                    float s = acc[t];
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                if (lane < a.n_peers)   // lane p stores the value into rank p's slot, region [rank]
-                    a.peer_out[lane][((size_t)a.rank * T + t) * a.D + d] = s;
+                    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                    if (lane == 0) own[d - d0][t] = s;
+                    if (lane < a.n_peers)   // lane p stores the value into rank p's slot, region [rank]
+                        s_out[lane][((size_t)a.rank * T + t) * a.D + d] = s;
+                }
             }
         }
     }
-    // every rank counts this CTA once its stores are visible system-wide: the barrier makes every
-    // thread's stores visible to thread 0, whose system-scope fence (cumulative) then orders them all
-    // before its counter increments (one fence per CTA: a fence in every thread cost ~6 us a launch)
+    // count the band on every rank once its stores are visible to that rank: the barrier orders every
+    // thread's stores before thread 0's release add (release is cumulative).  System scope across
+    // GPUs; with one rank nothing outside this GPU reads the slot, and GPU scope is the cheaper
+    // release (measured ~0.7 vs ~2.5 us)
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence_system();
-        for (int p = 0; p < a.n_peers; p++) atomicAdd_system(a.peer_ctr[p], 1u);
-        // wait (bounded) for every CTA of every rank of this epoch
-        const unsigned int target = (unsigned int)(*reinterpret_cast<const volatile int*>(a.epoch_dev)) *
-                                    (unsigned int)(a.n_peers * gridDim.x);
+        const bool sys = a.n_peers > 1;
+        for (int p = 0; p < a.n_peers; p++) {
+            if (sys) red_add_release_sys(s_bctr[p] + blockIdx.x, 1u);
+            else red_add_release_gpu(s_bctr[p] + blockIdx.x, 1u);
+        }
+        // wait (bounded) for this band of every rank of this epoch
+        const unsigned int target = s_target;
         const uint64_t t0 = globaltimer_ns();
-        bool ok = true;
-        while (*reinterpret_cast<const volatile unsigned int*>(a.my_ctr) < target) {
-            __nanosleep(64);   // every CTA polls this line while the others' atomics update it: back off
+        while ((sys ? ld_acquire_sys(a.my_bctr + blockIdx.x) : ld_acquire_gpu(a.my_bctr + blockIdx.x)) < target) {
             if (globaltimer_ns() - t0 > kWaitLimitNs) {
                 if (a.err) atomicOr(a.err, ERRBIT_TIMEOUT);
-                ok = false;
+                ok_flag = 0;
                 break;
             }
         }
-        __threadfence_system();
-        ok_flag = ok;
     }
     __syncthreads();
     if (!ok_flag) return;
-    // the band's sum over ranks, in rank order (identical on every rank)
-    for (int i = threadIdx.x; i < T * (d1 - d0); i += blockDim.x) {
-        const int t = i / (d1 - d0), d = d0 + i % (d1 - d0);
+    // the band's sum over ranks, in rank order (identical on every rank: this rank's own term is the
+    // value it stored into every slot, taken from shared memory)
+    for (int i = threadIdx.x; i < T * nb; i += blockDim.x) {
+        const int t = i / nb, d = d0 + i % nb;
         float s = 0.0f;
-        for (int r = 0; r < a.n_peers; r++) s += __ldcv(&a.my_slot[((size_t)r * T + t) * a.D + d]);
+        for (int r = 0; r < a.n_peers; r++)
+            s += r == a.rank ? own[d - d0][t] : __ldcv(&a.my_slot[((size_t)r * T + t) * a.D + d]);
         a.out[(size_t)t * a.D + d] = s;
     }
 }
@@ -185,23 +241,30 @@ cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st) {
     a.D = r.D;
     a.T = r.T;
     a.peer_out = r.peer_out;
-    a.peer_ctr = r.peer_ctr;
+    a.peer_bctr = r.peer_ctr;
     a.n_peers = r.n_peers;
     a.rank = r.rank;
-    a.my_ctr = r.my_ctr;
+    a.my_bctr = r.my_ctr;
     a.my_slot = r.my_slot;
     a.epoch_dev = r.epoch_dev;
     a.out = r.out;
     a.err = r.err;
-    const size_t smem = (size_t)r.T * r.K_local * sizeof(float);
-    static cudaError_t attr = cudaFuncSetAttribute(out_proj_peer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   kOpMaxT * 4096 * (int)sizeof(float));
+    static cudaError_t attr =
+        cudaFuncSetAttribute(out_proj_peer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOpSmemBytes);
     if (attr != cudaSuccess) return attr;
-    const int n_ctas = std::min(kNumSMs, std::max(1, r.D / 8));
-    // no programmatic early start of the next launch: this kernel's CTAs wait on one another
+    const int n_ctas = std::min(std::min(kNumSMs, kPeerBands), std::max(1, r.D / 8));
+    const int band_max = (r.D + n_ctas - 1) / n_ctas;
+    // x as f32 (T x K_local x 4 <= 128 KB), then as many whole weight rows as the rest holds
+    a.w_off = (uint32_t)(((size_t)r.T * r.K_local * sizeof(float) + 127) & ~(size_t)127);
+    const size_t row_bytes = (size_t)r.K_local * 2;
+    const size_t fit = ((size_t)kOpSmemBytes - a.w_off) / row_bytes;
+    a.rows_per_round = (int)std::min(fit, (size_t)std::min(kOpMaxRows, band_max));
+    const size_t smem = a.w_off + (size_t)a.rows_per_round * row_bytes;
     return launch_pdl(out_proj_peer_kernel, dim3((unsigned)n_ctas), dim3(kOpThreads), smem, st, a);
 }
 
 int out_proj_max_t() { return kOpMaxT; }
+int out_proj_max_d() { return kNumSMs * kOpMaxBand; }
 
 }  // namespace svkv
+

@@ -57,11 +57,13 @@ int sv_peer_create(int device, int rank, int world, int n_slots, size_t slot_byt
     p->n_slots = n_slots;
     p->slot_bytes = slot_bytes;
     p->ctr_off = ((size_t)n_slots * slot_bytes + 255) & ~(size_t)255;
-    p->buf_bytes = p->ctr_off + (((size_t)n_slots * sizeof(unsigned int) + 255) & ~(size_t)255);
+    p->bctr_off = p->ctr_off + (((size_t)n_slots * sizeof(unsigned int) + 255) & ~(size_t)255);
+    p->buf_bytes = p->bctr_off + (size_t)n_slots * svkv::kPeerBands * sizeof(unsigned int);
     bool ok = cudaMalloc(&p->buf, p->buf_bytes) == cudaSuccess;
     ok = ok && cudaMemset(p->buf, 0, p->buf_bytes) == cudaSuccess;
     ok = ok && cudaMalloc(&p->d_out, sizeof(float*) * n_slots * world) == cudaSuccess;
     ok = ok && cudaMalloc(&p->d_ctr, sizeof(unsigned int*) * n_slots * world) == cudaSuccess;
+    ok = ok && cudaMalloc(&p->d_bctr, sizeof(unsigned int*) * n_slots * world) == cudaSuccess;
     ok = ok && cudaDeviceSynchronize() == cudaSuccess;
     cudaSetDevice(prev);
     if (!ok) {
@@ -69,6 +71,7 @@ int sv_peer_create(int device, int rank, int world, int n_slots, size_t slot_byt
         if (p->buf) cudaFree(p->buf);
         if (p->d_out) cudaFree(p->d_out);
         if (p->d_ctr) cudaFree(p->d_ctr);
+        if (p->d_bctr) cudaFree(p->d_bctr);
         delete p;
         return SV_ERR_NOMEM;
     }
@@ -114,17 +117,22 @@ int sv_peer_import(sv_peer* p, const void* handles) {
         const int n = p->n_slots * p->world;
         float** h_out = new float*[n];
         unsigned int** h_ctr = new unsigned int*[n];
+        unsigned int** h_bctr = new unsigned int*[n];
         for (int s = 0; s < p->n_slots; s++) {
             for (int r = 0; r < p->world; r++) {
                 h_out[s * p->world + r] = reinterpret_cast<float*>(p->base[r] + (size_t)s * p->slot_bytes);
                 h_ctr[s * p->world + r] = reinterpret_cast<unsigned int*>(p->base[r] + p->ctr_off) + s;
+                h_bctr[s * p->world + r] =
+                    reinterpret_cast<unsigned int*>(p->base[r] + p->bctr_off) + (size_t)s * svkv::kPeerBands;
             }
         }
         if (cudaMemcpy(p->d_out, h_out, sizeof(float*) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
-            cudaMemcpy(p->d_ctr, h_ctr, sizeof(unsigned int*) * n, cudaMemcpyHostToDevice) != cudaSuccess)
+            cudaMemcpy(p->d_ctr, h_ctr, sizeof(unsigned int*) * n, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(p->d_bctr, h_bctr, sizeof(unsigned int*) * n, cudaMemcpyHostToDevice) != cudaSuccess)
             rc = SV_ERR_CUDA;
         delete[] h_out;
         delete[] h_ctr;
+        delete[] h_bctr;
     }
     cudaSetDevice(prev);
     if (rc == SV_OK) p->imported = true;
@@ -157,7 +165,7 @@ int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, cons
     if (x_type != SV_TYPE_F16 && x_type != SV_TYPE_F32) return SV_ERR_UNSUPPORTED;
     // 16-byte weight loads: row starts and the column slice on 8-element boundaries; x staged in
     // shared memory (T x K_local f32 <= 128 KB)
-    if (T > svkv::out_proj_max_t() || (K_total & 7) || (k_offset & 7) || (K_local & 7) || K_local > 4096 ||
+    if (T > svkv::out_proj_max_t() || D > svkv::out_proj_max_d() || (K_total & 7) || (k_offset & 7) || (K_local & 7) || K_local > 4096 ||
         (reinterpret_cast<uintptr_t>(w) & 15))
         return SV_ERR_UNSUPPORTED;
     if ((size_t)p->world * T * D * sizeof(float) > p->slot_bytes) return SV_ERR_INVALID;
@@ -176,10 +184,10 @@ int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, cons
     r.D = D;
     r.T = T;
     r.peer_out = p->d_out + (size_t)slot * p->world;
-    r.peer_ctr = p->d_ctr + (size_t)slot * p->world;
+    r.peer_ctr = p->d_bctr + (size_t)slot * p->world;
     r.n_peers = p->world;
     r.rank = p->rank;
-    r.my_ctr = p->ctr(slot);
+    r.my_ctr = p->bctr(slot);
     r.my_slot = reinterpret_cast<const float*>(p->buf + (size_t)slot * p->slot_bytes);
     r.epoch_dev = epoch_dev;
     r.out = out;
@@ -200,6 +208,7 @@ int sv_peer_destroy(sv_peer* p) {
     if (p->buf) cudaFree(p->buf);
     if (p->d_out) cudaFree(p->d_out);
     if (p->d_ctr) cudaFree(p->d_ctr);
+    if (p->d_bctr) cudaFree(p->d_bctr);
     cudaSetDevice(prev);
     delete p;
     return SV_OK;
