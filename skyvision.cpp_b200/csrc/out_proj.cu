@@ -21,9 +21,10 @@
 //      ranks in rank order, so every rank ends with bitwise the same output.
 // A CTA waits only for the same band of the other ranks.  The grid never exceeds one CTA per SM,
 // so every CTA of a launch is resident while any of them waits; the next launch is let in once the
-// whole grid runs (its CTAs take SMs as these exit and issue their own weight rows meanwhile).  A slot holds [world][T][D] f32
-// partials; a slot is rewritten only after every rank has summed it when consecutive layers use
-// different slots (a rank reaches layer l + 2 only after every rank finished layer l).
+// whole grid runs (its CTAs take SMs as these exit and issue their own weight rows meanwhile).
+// A slot holds [world][T][D] f32 partials; a slot is rewritten only after every rank has summed it
+// when consecutive layers use different slots (a rank reaches layer l + 2 only after every rank
+// finished layer l).
 //
 // Bound: HBM on the weights (D x K_local x 2 bytes per launch) plus two NVLink latencies.
 #include "common.cuh"
