@@ -363,7 +363,9 @@ int sv_peer_destroy(sv_peer* p);
  * it with the same D, T and slot; slot_bytes >= world * T * D * 4.  Like the attention gather,
  * each slot is used once per epoch (one slot per layer; *epoch_dev counts steps from 1 and the
  * caller advances it after each step), so consecutive calls use different slots.  T <= 8,
- * K_local <= 4096 and multiples of 8, D <= 18944.  No reference counterpart (the
+ * K_local <= 4096 and multiples of 8, D <= 18944.  w is read before the kernel's dependency on
+ * the previous kernel of the stream: weights written on the GPU must be complete before that
+ * kernel starts.  No reference counterpart (the
  * reference runs one process per model); replaces an NCCL all-gather of the attention rows
  * followed by the full projection on every rank. */
 int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, const void* w, int K_total, int k_offset,
