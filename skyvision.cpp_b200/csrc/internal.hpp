@@ -194,10 +194,10 @@ struct OutProjLaunch {
     int64_t x_nb_t;
     const uint16_t* w;
     int K_total, k_offset, K_local, D, T;
-    float* const* peer_out;
-    unsigned int* const* peer_ctr;
+    float* const* peer_out;            // the slot's region on every rank [world]
+    unsigned int* const* peer_bctr;    // the slot's band counters on every rank [world]
     int n_peers, rank;
-    const unsigned int* my_ctr;        // this rank's band counters of the slot [kPeerBands]
+    const unsigned int* my_bctr;       // this rank's band counters of the slot [kPeerBands]
     const float* my_slot;
     const int32_t* epoch_dev;
     float* out;

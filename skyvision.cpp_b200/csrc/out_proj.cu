@@ -242,10 +242,10 @@ cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st) {
     a.D = r.D;
     a.T = r.T;
     a.peer_out = r.peer_out;
-    a.peer_bctr = r.peer_ctr;
+    a.peer_bctr = r.peer_bctr;
     a.n_peers = r.n_peers;
     a.rank = r.rank;
-    a.my_bctr = r.my_ctr;
+    a.my_bctr = r.my_bctr;
     a.my_slot = r.my_slot;
     a.epoch_dev = r.epoch_dev;
     a.out = r.out;

@@ -184,10 +184,10 @@ int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, cons
     r.D = D;
     r.T = T;
     r.peer_out = p->d_out + (size_t)slot * p->world;
-    r.peer_ctr = p->d_bctr + (size_t)slot * p->world;
+    r.peer_bctr = p->d_bctr + (size_t)slot * p->world;
     r.n_peers = p->world;
     r.rank = p->rank;
-    r.my_ctr = p->bctr(slot);
+    r.my_bctr = p->bctr(slot);
     r.my_slot = reinterpret_cast<const float*>(p->buf + (size_t)slot * p->slot_bytes);
     r.epoch_dev = epoch_dev;
     r.out = out;
