@@ -144,3 +144,22 @@ def test_invalid_arguments_rejected():
     assert L.sv_kv_destroy(None) == -1
     assert L.sv_attn(None, 0, None, 1, 1, 32, 0, 1.0, None, None) == -1
     assert L.sv_set_rows(None, 1, 16, 4, 32, None, 1, 32, 1, None, 0, None, None) == -1
+
+
+def test_peer_and_projection_arguments_rejected():
+    """The peer-group and sharded-projection entry points refuse bad arguments before any CUDA call
+    (world outside 1..8, rank outside the world, no slots, slot sizes that are not 16-byte multiples,
+    null handles)."""
+    L = sv.lib()
+    h = ctypes.c_void_p()
+    for dev, rank, world, n_slots, slot_bytes in [(0, 0, 0, 1, 16), (0, 0, 9, 1, 16), (0, 2, 2, 1, 16),
+                                                  (0, -1, 2, 1, 16), (0, 0, 1, 0, 16), (0, 0, 1, 1, 10),
+                                                  (0, 0, 1, 1, 0)]:
+        assert L.sv_peer_create(dev, rank, world, n_slots, slot_bytes, ctypes.byref(h)) == -1
+        assert not h.value
+    assert L.sv_peer_create(0, 0, 1, 1, 16, None) == -1
+    assert L.sv_peer_destroy(None) == 0
+    assert L.sv_peer_wait(None, 0, None, 1, None, None) == -1
+    assert L.sv_out_proj_peer(None, None, 1, 8192, None, 4096, 0, 4096, 2560, 1, 0, None, None, None, None) == -1
+    assert L.sv_qk_norm_rope_append(None, 0, None, None, None, 1, 32, None, None, 1e-6, None, None, 0, None, None,
+                                    1, None) == -1
