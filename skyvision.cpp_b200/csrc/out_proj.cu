@@ -141,10 +141,13 @@ __global__ void __launch_bounds__(kOpThreads, 1) out_proj_peer_kernel(const __gr
         }
     }
     __syncthreads();
+    int last_issued = 0;   // the round whose copies were issued last (uniform across the CTA)
     for (int round = 0; round < n_rounds; round++) {
         if (round > 0) {
             __syncthreads();   // every warp is done with the previous round's rows
+            if (!ok_flag) break;   // a row of that round never landed: issue nothing more
             if (warp == 0) issue(round);
+            last_issued = round;
         }
         const int r0 = round * RR, n = min(RR, nb - r0);
         for (int i = warp; i < n; i += kOpWarps) {
@@ -198,6 +201,12 @@ __global__ void __launch_bounds__(kOpThreads, 1) out_proj_peer_kernel(const __gr
     // release (measured ~0.7 vs ~2.5 us)
     __syncthreads();
     if (threadIdx.x == 0) {
+        if (!ok_flag) {
+            // a row never landed (the error bit is set): before the CTA leaves, wait (bounded) for the
+            // last round's copies that may still be in flight into its shared memory
+            const int n_last = min(RR, nb - last_issued * RR);
+            for (int i = 0; i < n_last; i++) mbar_wait_limit(&full[i], last_issued & 1, nullptr, kWaitLimitNs);
+        }
         const bool sys = a.n_peers > 1;
         for (int p = 0; p < a.n_peers; p++) {
             if (sys) red_add_release_sys(s_bctr[p] + blockIdx.x, 1u);
