@@ -656,18 +656,19 @@ fa_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant_
     if (tid == 0) a.tickets[tile] = 0;
 }
 
-// one-time kernel attributes: dynamic shared memory and clusters of up to 16 CTAs
+// kernel attributes, once per device: dynamic shared memory and clusters of up to 16 CTAs
 template <int HD, int KVT>
 cudaError_t prepare_t() {
-    static cudaError_t status = [] {
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t status[kMaxDevices];
+    return once_per_device(once, status, [] {
         using C = DecCfg<HD, KVT>;
         cudaError_t e = cudaFuncSetAttribute(fa_decode_kernel<HD, KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              C::SMEM + 1024);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(fa_decode_kernel<HD, KVT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         return e;
-    }();
-    return status;
+    });
 }
 
 template <int HD, int KVT>

@@ -842,17 +842,19 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     if (c == 0) st_async_f2(dsmem_map(smem_u32(&slot_ml[(split * C::ROWS_MAX + r) * 2]), 0), make_float2(M, L), bar);
 }
 
+// kernel attributes, once per device
 template <int HD, int KVT, bool kPeer = false>
 cudaError_t prepare_gqa() {
-    static cudaError_t status = [] {
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t status[kMaxDevices];
+    return once_per_device(once, status, [] {
         cudaError_t e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, GqaCfg<HD, KVT>::SMEM + 1024);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer>,
                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         return e;
-    }();
-    return status;
+    });
 }
 
 template <int HD, int KVT, bool kPeer>

@@ -708,9 +708,12 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     }
 }
 
+// kernel attributes, once per device
 template <int HD, int NQT, int NP, int PL>
 cudaError_t prepare_t() {
-    static cudaError_t status = [] {
+    static std::once_flag once[kMaxDevices];
+    static cudaError_t status[kMaxDevices];
+    return once_per_device(once, status, [] {
         using C = PreCfg<HD, NQT, NP>;
         cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM + 1024);
@@ -718,8 +721,7 @@ cudaError_t prepare_t() {
             e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL>, cudaFuncAttributeNonPortableClusterSizeAllowed,
                                      1);
         return e;
-    }();
-    return status;
+    });
 }
 
 // Splits of the key range per CTA (one CTA per SM, no clusters): minimise (waves) x (per-CTA

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <vector>
 
 #include "../../include/svkv.h"
@@ -25,6 +26,20 @@ inline size_t row_bytes_of(int type, int64_t ne0) {
 }
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// Runs init() once per device (the current one) and returns its cached status.  Kernel attributes
+// (dynamic shared memory above 48 KB, non-portable cluster sizes) belong to a device's context, so a
+// process that drives several GPUs must set them on each.
+constexpr int kMaxDevices = 64;
+template <class F>
+cudaError_t once_per_device(std::once_flag (&once)[kMaxDevices], cudaError_t (&status)[kMaxDevices], F&& init) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(once[dev], [&] { status[dev] = init(); });
+    return status[dev];
+}
 
 // ------------------------------------------------------------ attention args
 // One attention launch: queries x one kv view.  All strides in bytes.

@@ -259,8 +259,11 @@ cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st) {
     a.epoch_dev = r.epoch_dev;
     a.out = r.out;
     a.err = r.err;
-    static cudaError_t attr =
-        cudaFuncSetAttribute(out_proj_peer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOpSmemBytes);
+    static std::once_flag once[kMaxDevices];   // the attribute, once per device
+    static cudaError_t status[kMaxDevices];
+    const cudaError_t attr = once_per_device(once, status, [] {
+        return cudaFuncSetAttribute(out_proj_peer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOpSmemBytes);
+    });
     if (attr != cudaSuccess) return attr;
     const int n_ctas = std::min(std::min(kNumSMs, kPeerBands), std::max(1, r.D / 8));
     const int band_max = (r.D + n_ctas - 1) / n_ctas;
