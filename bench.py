@@ -480,7 +480,7 @@ def run_svkv(args, world, rank, local):
         line["batched"] = batched
     line.update(extras)
     if world == 1 and not args.no_cpu_baseline:
-        n_layers, n_tok = 8, 12
+        n_layers, n_tok = 8, 48
         per_tl, cores = cpu_decode_sample(n_layers, n_tok)
         line["cpu_baseline"] = {
             "value": 1.0 / (per_tl * L), "unit": "tokens/s", "cores": cores, "kind": "port",

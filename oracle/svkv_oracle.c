@@ -20,7 +20,9 @@
  *                       qwen3vl_model.cpp:657-663; GQA head map kv = h / (NH/NKV);
  *                       masks: set_causal_mask attention.hpp:60-67, set_window_mask
  *                       attention.hpp:71-83, or an explicit additive f16 mask;
- *                       fp32 accumulation (two-pass softmax per query row)
+ *                       fp32 accumulation (two-pass softmax per query row; each q.k dot
+ *                       product in 8 interleaved partial sums, as ggml's SIMD vec_dot
+ *                       keeps several accumulators)
  *   orc_can_splice      KV splice predicate                                  qwen3vl_model.cpp:1165-1171
  *   orc_evict_window    sliding-window kept-set rule                         qwen3vl_model.cpp:1110-1124,
  *                                                                            mage_model.cpp:1827-1841
@@ -29,9 +31,10 @@
  *                       reference names no generator for these configs, so this
  *                       one is documented and shared with the bench.
  *
- * Build: make -C oracle   (gcc -O2 -fopenmp, shared library)
+ * Build: make -C oracle   (gcc -O3 -fopenmp, no fast-math, no FMA contraction; shared library)
  */
 #include <math.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -237,6 +240,27 @@ int orc_set_rows(void* dst, int dst_type, int64_t ne0, int64_t dst_rows, size_t 
 }
 
 /* ---------------------------------------------------------------- attention */
+/* every f16 value as f32 (the exact conversion above, tabulated once) */
+static float g_f16_f32[65536];
+static pthread_once_t g_f16_once = PTHREAD_ONCE_INIT;
+static void f16_table_fill(void) {
+    for (uint32_t h = 0; h < 65536u; h++) g_f16_f32[h] = orc_f16_to_f32((uint16_t)h);
+}
+
+/* the dequantised K/V view, kept between calls (a fresh 2 x 37 MB buffer per decode layer spent as
+ * much time in page faults as in the arithmetic); calls are serialised on its lock */
+static pthread_mutex_t g_kv_mu = PTHREAD_MUTEX_INITIALIZER;
+static float* g_kv_buf = NULL;
+static size_t g_kv_floats = 0;
+static float* kv_buffer(size_t n_floats) {
+    if (n_floats > g_kv_floats) {
+        free(g_kv_buf);
+        g_kv_buf = (float*)malloc(n_floats * sizeof(float));
+        g_kv_floats = g_kv_buf ? n_floats : 0;
+    }
+    return g_kv_buf;
+}
+
 /* q: f32 [T][NH][HD] (row stride q_nb1 floats between queries, NH*HD when packed)
  * k, v: cache views; key s of kv-head g starts at base + s*kv_nb1 + g*head_bytes
  *       where head_bytes = row_bytes_of(kv_type, HD).
@@ -256,15 +280,33 @@ int orc_attn(const float* q, int64_t q_nb1, int T, int NH, int HD,
     const int grp = NH / NKV;
     const size_t head_bytes = row_bytes_of(kv_type, HD);
     /* dequantise the whole view once per kv head: kf/vf [NKV][S][HD] */
-    float* kf = (float*)malloc((size_t)NKV * S * HD * sizeof(float));
-    float* vf = (float*)malloc((size_t)NKV * S * HD * sizeof(float));
+    pthread_once(&g_f16_once, f16_table_fill);
+    pthread_mutex_lock(&g_kv_mu);
+    const size_t view_floats = (size_t)NKV * S * HD;
+    float* kf = kv_buffer(2 * view_floats + 1);
+    if (!kf) {
+        pthread_mutex_unlock(&g_kv_mu);
+        return -3;
+    }
+    float* vf = kf + view_floats;
 #pragma omp parallel for schedule(static)
     for (int64_t idx = 0; idx < (int64_t)NKV * S; idx++) {
         const int g = (int)(idx / S), s = (int)(idx % S);
         const uint8_t* kr = (const uint8_t*)k + (size_t)s * kv_nb1 + (size_t)g * head_bytes;
         const uint8_t* vr = (const uint8_t*)v + (size_t)s * kv_nb1 + (size_t)g * head_bytes;
-        load_row_f32(kr, kv_type, HD, kf + ((size_t)g * S + s) * HD);
-        load_row_f32(vr, kv_type, HD, vf + ((size_t)g * S + s) * HD);
+        float* kd = kf + ((size_t)g * S + s) * HD;
+        float* vd = vf + ((size_t)g * S + s) * HD;
+        if (kv_type == ORC_TYPE_F16) {
+            const uint16_t* kh = (const uint16_t*)kr;
+            const uint16_t* vh = (const uint16_t*)vr;
+            for (int e = 0; e < HD; e++) {
+                kd[e] = g_f16_f32[kh[e]];
+                vd[e] = g_f16_f32[vh[e]];
+            }
+        } else {
+            load_row_f32(kr, kv_type, HD, kd);
+            load_row_f32(vr, kv_type, HD, vd);
+        }
     }
 #pragma omp parallel
     {
@@ -287,8 +329,12 @@ int orc_attn(const float* q, int64_t q_nb1, int T, int NH, int HD,
                 }
                 if (!vis) { sc[s] = -INFINITY; continue; }
                 const float* kr = kf + ((size_t)g * S + s) * HD;
-                float dot = 0.0f;
-                for (int e = 0; e < HD; e++) dot += qr[e] * kr[e];
+                float a8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+                int e = 0;
+                for (; e + 8 <= HD; e += 8)
+                    for (int j = 0; j < 8; j++) a8[j] += qr[e + j] * kr[e + j];
+                float dot = ((a8[0] + a8[4]) + (a8[1] + a8[5])) + ((a8[2] + a8[6]) + (a8[3] + a8[7]));
+                for (; e < HD; e++) dot += qr[e] * kr[e];
                 sc[s] = dot * scale + add;
                 if (sc[s] > m) m = sc[s];
             }
@@ -311,8 +357,7 @@ int orc_attn(const float* q, int64_t q_nb1, int T, int NH, int HD,
         free(sc);
         free(acc);
     }
-    free(kf);
-    free(vf);
+    pthread_mutex_unlock(&g_kv_mu);
     return 0;
 }
 
