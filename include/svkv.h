@@ -170,7 +170,9 @@ int sv_flash_attn_ext(const sv_fa_params* p, void* workspace, size_t ws_bytes, v
  * before any stream capture.  Shapes that need more than 4 MiB of scratch
  * return SV_ERR_WORKSPACE.  The array is shared by all calls and keeps the last
  * call's contents (the merge tickets are cleared on each call); calls that
- * overlap on the GPU race. */
+ * overlap on the GPU race.  The cached address belongs to the device's primary
+ * context: after cudaDeviceReset (or any reset of that context) the library
+ * must be unloaded and loaded again before this entry point is used. */
 int sv_flash_attn_ext_static(const sv_fa_params* p, void* stream);
 
 /* Cache-level attention for one decoder layer (the FA node of
@@ -365,7 +367,12 @@ int sv_peer_destroy(sv_peer* p);
  * caller advances it after each step), so consecutive calls use different slots.  T <= 8,
  * K_local <= 4096 and multiples of 8, D <= 18944.  w is read before the kernel's dependency on
  * the previous kernel of the stream: weights written on the GPU must be complete before that
- * kernel starts.  No reference counterpart (the
+ * kernel starts.  The grid is at most one CTA per SM of the device and every CTA waits for the same
+ * band of every rank, so all CTAs must be resident at once: a process restricted to a share of the
+ * SMs (MPS, green contexts) gets SV_DEVERR_TIMEOUT instead of a result.  If one rank's wait for its
+ * own weight rows expires, it does not count its band on any rank, so every rank reports
+ * SV_DEVERR_TIMEOUT (no rank sums a stale partial); the peer group must then be recreated.
+ * No reference counterpart (the
  * reference runs one process per model); replaces an NCCL all-gather of the attention rows
  * followed by the full projection on every rank. */
 int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, const void* w, int K_total, int k_offset,

@@ -188,7 +188,9 @@ __device__ __forceinline__ void signal_peers(const AttnArgs& a, int bar_id, int 
 __device__ __forceinline__ void wait_gather(const AttnArgs& a) {
     const unsigned int target = (unsigned int)(*reinterpret_cast<const volatile int*>(a.epoch_dev)) * a.wait_per_epoch;
     const uint64_t t0 = globaltimer_ns();
-    while (*reinterpret_cast<const volatile unsigned int*>(a.wait_ctr) < target) {
+    // acquire loads: the peers' rows, stored before their release of the counter, are visible to every
+    // read this CTA makes after the barrier that follows
+    while (ld_acquire_sys(a.wait_ctr) < target) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             if (a.err) atomicOr(a.err, ERRBIT_TIMEOUT);
             break;

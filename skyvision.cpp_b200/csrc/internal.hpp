@@ -41,6 +41,19 @@ cudaError_t once_per_device(std::once_flag (&once)[kMaxDevices], cudaError_t (&s
     return status[dev];
 }
 
+// SM count of the current device (cached per device); kNumSMs when the query fails
+inline int device_sm_count() {
+    static std::once_flag once[kMaxDevices];
+    static int count[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return kNumSMs;
+    std::call_once(once[dev], [&] {
+        int n = 0;
+        count[dev] = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0 ? n : kNumSMs;
+    });
+    return count[dev];
+}
+
 // ------------------------------------------------------------ attention args
 // One attention launch: queries x one kv view.  All strides in bytes.
 struct AttnArgs {

@@ -203,23 +203,28 @@ __global__ void __launch_bounds__(kOpThreads, 1) out_proj_peer_kernel(const __gr
     if (threadIdx.x == 0) {
         if (!ok_flag) {
             // a row never landed (the error bit is set): before the CTA leaves, wait (bounded) for the
-            // last round's copies that may still be in flight into its shared memory
+            // last round's copies that may still be in flight into its shared memory.  The band is not
+            // counted on any rank: this rank's partials in the peers' slots are stale, so the peers'
+            // bounded waits expire and they report the timeout too instead of summing stale values.
+            // The counters then stay one arrival short, so every later epoch of this peer group times
+            // out as well: the group has to be recreated.
             const int n_last = min(RR, nb - last_issued * RR);
             for (int i = 0; i < n_last; i++) mbar_wait_limit(&full[i], last_issued & 1, nullptr, kWaitLimitNs);
-        }
-        const bool sys = a.n_peers > 1;
-        for (int p = 0; p < a.n_peers; p++) {
-            if (sys) red_add_release_sys(s_bctr[p] + blockIdx.x, 1u);
-            else red_add_release_gpu(s_bctr[p] + blockIdx.x, 1u);
-        }
-        // wait (bounded) for this band of every rank of this epoch
-        const unsigned int target = s_target;
-        const uint64_t t0 = globaltimer_ns();
-        while ((sys ? ld_acquire_sys(a.my_bctr + blockIdx.x) : ld_acquire_gpu(a.my_bctr + blockIdx.x)) < target) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs) {
-                if (a.err) atomicOr(a.err, ERRBIT_TIMEOUT);
-                ok_flag = 0;
-                break;
+        } else {
+            const bool sys = a.n_peers > 1;
+            for (int p = 0; p < a.n_peers; p++) {
+                if (sys) red_add_release_sys(s_bctr[p] + blockIdx.x, 1u);
+                else red_add_release_gpu(s_bctr[p] + blockIdx.x, 1u);
+            }
+            // wait (bounded) for this band of every rank of this epoch
+            const unsigned int target = s_target;
+            const uint64_t t0 = globaltimer_ns();
+            while ((sys ? ld_acquire_sys(a.my_bctr + blockIdx.x) : ld_acquire_gpu(a.my_bctr + blockIdx.x)) < target) {
+                if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    if (a.err) atomicOr(a.err, ERRBIT_TIMEOUT);
+                    ok_flag = 0;
+                    break;
+                }
             }
         }
     }
@@ -265,7 +270,9 @@ cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st) {
         return cudaFuncSetAttribute(out_proj_peer_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kOpSmemBytes);
     });
     if (attr != cudaSuccess) return attr;
-    const int n_ctas = std::min(std::min(kNumSMs, kPeerBands), std::max(1, r.D / 8));
+    // one CTA per SM at most: a CTA waits for the same band of every rank, so all of them must be
+    // resident at once (the device's own SM count; a share of the SMs under MPS can still time out)
+    const int n_ctas = std::min(std::min(device_sm_count(), kPeerBands), std::max(1, r.D / 8));
     const int band_max = (r.D + n_ctas - 1) / n_ctas;
     // x as f32 (T x K_local x 4 <= 128 KB), then as many whole weight rows as the rest holds
     a.w_off = (uint32_t)(((size_t)r.T * r.K_local * sizeof(float) + 127) & ~(size_t)127);

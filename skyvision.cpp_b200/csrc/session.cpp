@@ -105,7 +105,9 @@ int sv_session_reset(sv_session* s) {
 int sv_session_begin_turn(sv_session* s, int n_new_frames, int* first_row, int* kept_new_frames, void* stream) {
     if (!s || n_new_frames < 0 || s->open) return SV_ERR_INVALID;
     const int rpf = s->rows_per_frame;
-    s->n_marks += n_new_frames;
+    // the frame count is worked out in a local and written back only once the compaction succeeded,
+    // so a failed call leaves the session as it was
+    int n_marks = s->n_marks + n_new_frames;
     int new_kept = n_new_frames;
 
     // ---- the window rule on the turn table
@@ -113,15 +115,15 @@ int sv_session_begin_turn(sv_session* s, int n_new_frames, int* first_row, int* 
     std::vector<sv_segment> segs;
     if (s->sink_rows > 0) segs.push_back({0, s->sink_rows, 1});
     size_t drop_turns = 0;
-    while (s->n_marks > s->max_frames && s->turns.size() - drop_turns > 1) {
+    while (n_marks > s->max_frames && s->turns.size() - drop_turns > 1) {
         const sv_session::Turn& t = s->turns[drop_turns];
-        s->n_marks -= t.frames;
+        n_marks -= t.frames;
         segs.push_back({t.start, t.rows(rpf), 0});
         drop_turns++;
     }
     int trim = 0;   // frames trimmed from the (new) front turn
-    while (s->n_marks > s->max_frames) {
-        s->n_marks--;
+    while (n_marks > s->max_frames) {
+        n_marks--;
         if (drop_turns < s->turns.size() && s->turns[drop_turns].frames - trim > 0) trim++;
         else if (new_kept > 0) new_kept--;
     }
@@ -159,6 +161,7 @@ int sv_session_begin_turn(sv_session* s, int n_new_frames, int* first_row, int* 
         fprintf(stderr, "session: evicted %d rows (%zu turns, %d frames), %d live\n", n_before - new_len,
                 drop_turns, trim, new_len);
     }
+    s->n_marks = n_marks;
     s->open = true;
     s->open_frames = new_kept;
     if (first_row) *first_row = (int)s->row_ids.size();

@@ -5,8 +5,8 @@ code running during CUDA stream capture may not call cudaMalloc, so neither can
 hand sv_flash_attn_ext a workspace.  The static entry point keeps the split-K
 scratch in a fixed device array of the library.  This test calls it through
 the C ABI twice in a row and checks each result against sv_flash_attn_ext with
-a caller-allocated workspace, within the attention tolerance of the other
-tests; it also checks that a shape needing more scratch than the array holds
+a caller-allocated workspace and against the CPU oracle, within the attention
+tolerance of the other tests; it also checks that a shape needing more scratch than the array holds
 is refused.  (This file is named so that pytest collects it last.)
 """
 import ctypes
@@ -54,7 +54,7 @@ def _check_close(got, ref):
     assert d.max() <= MAX_ABS and rel <= REL_L2, (float(d.max()), float(rel))
 
 
-def test_static_scratch_matches_workspace_entry_point():
+def test_static_scratch_matches_workspace_entry_point(orc):
     NKV, HD, NH, S = 8, 128, 32, 3000          # one decode query: 8 kv heads x many key splits
     g = torch.Generator(device=DEV).manual_seed(7)
     static_fn = _static_fn()
@@ -75,6 +75,11 @@ def test_static_scratch_matches_workspace_entry_point():
         assert static_fn(ctypes.byref(p_st), stream) == 0
         torch.cuda.synchronize()
         _check_close(out_st.cpu().numpy(), out_ws.cpu().numpy())
+        # and both against the fp32-accumulated oracle (no mask: every key of the view is visible)
+        ref = orc.attn(q.float().cpu().numpy(), kb.cpu().numpy(), vb.cpu().numpy(), orc.TYPE_F16, NKV, HD, S,
+                       1 / np.sqrt(HD), orc.MASK_NONE)
+        _check_close(out_st.cpu().numpy(), ref)
+        _check_close(out_ws.cpu().numpy(), ref)
 
 
 def test_static_scratch_refuses_oversized_shape():
