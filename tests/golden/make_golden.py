@@ -31,7 +31,7 @@ What pins what:
   pairs 61 and 62 from the fourth (slot) stream, which HF takes from t; the
   fixture's slot stream equals t (a text-only turn), where both agree.
 
-Usage:  python tests/golden/make_golden.py [--reference /root/reference]
+Usage:  python tests/golden/make_golden.py --reference DIR   (or SVKV_REFERENCE=DIR)
 """
 from __future__ import annotations
 
@@ -79,7 +79,8 @@ def load_module(path: str, name: str):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SVKV_REFERENCE"),
+                    help="the reference checkout (default: $SVKV_REFERENCE)")
     ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
     args = ap.parse_args()
 
