@@ -220,6 +220,38 @@ int sv_soft_max_ext(const float* x, int64_t ne0, int64_t n_rows, size_t x_nb1, c
                     int64_t mask_rows, size_t mask_nb1, float scale, float* y, size_t y_nb1,
                     void* stream);
 
+/* The two mul_mat legs of that fallback (gemma4_model.cpp:685-691; moondream.cpp:476-493 runs
+ * them per head: n_kv_head = n_head = 1 over a one-head view), on the tensor cores.
+ *
+ * sv_mul_mat_kq replaces kq = ggml_mul_mat(kf, qf) (gemma4_model.cpp:685): the raw scores
+ *   kq[s, t, h] = sum_e k[e, s, h / (NH/NKV)] * q[e, t, h]   (ggml's broadcast of src0 over dim 2)
+ *   k   F16 cache view [HD, S, NKV]: key s of kv head g at k + s*k_nb1 + g*HD*2 (heads packed in
+ *       the row; k and k_nb1 16-byte aligned)
+ *   q   [HD, T, NH] of q_type (F16 or F32): element (e, t, h) at q + t*q_nb1 + h*q_nb2 + e*size
+ *       (16-byte aligned rows); an F32 query is rounded to f16 first, as ggml converts src1 to
+ *       the f16 vec-dot type of an F16 src0
+ *   kq  F32 [S, T, NH], contiguous (ggml's mul_mat result)
+ * head_dim 64, 128 or 256; n_head / n_kv_head <= 16. */
+int sv_mul_mat_kq(const void* k, size_t k_nb1, int n_kv_head, int head_dim, int n_keys, const void* q, int q_type,
+                  size_t q_nb1, size_t q_nb2, int T, int n_head, float* kq, void* stream);
+
+/* sv_mul_mat_kqv replaces vt = ggml_cont(ggml_transpose(vf)); kqv = ggml_mul_mat(vt, kq)
+ * (gemma4_model.cpp:689-690) and the permute + cont after it (:691), reading V in its cache
+ * layout (the transposed copy is never made):
+ *   kqv[e, t, h] = sum_s v[e, s, h / (NH/NKV)] * kq[s, t, h]
+ *   v   F16 cache view [HD, S, NKV], laid out like k above
+ *   kq  F32 [S, T, NH]: (s, t, h) at kq + t*kq_nb1 + h*kq_nb2 + 4*s (any row stride)
+ *   dst F32: (e, t, h) at dst + t*dst_nb1 + h*dst_nb2 + 4*e (16-byte aligned): ggml's
+ *       [HD, T, NH] result is dst_nb1 = HD*4, dst_nb2 = T*HD*4; the permuted [HD, NH, T] that
+ *       gemma4 reshapes to [NH*HD, T] is dst_nb1 = NH*HD*4, dst_nb2 = HD*4
+ * kq enters the tensor core as f16 hi + lo parts (~22 bits kept).  The key range is split over
+ * the SMs when `workspace` holds sv_mul_mat_kqv_workspace(...) bytes (0 = unsplit; a smaller
+ * workspace gives fewer splits).  head_dim 64, 128 or 256; n_head / n_kv_head <= 16. */
+size_t sv_mul_mat_kqv_workspace(int n_kv_head, int head_dim, int n_keys, int T, int n_head);
+int sv_mul_mat_kqv(const void* v, size_t v_nb1, int n_kv_head, int head_dim, int n_keys, const float* kq,
+                   size_t kq_nb1, size_t kq_nb2, int T, int n_head, float* dst, size_t dst_nb1, size_t dst_nb2,
+                   void* workspace, size_t ws_bytes, void* stream);
+
 /* ================================================================ eviction
  * In-HBM, order-preserving compaction of every layer's K and V
  * (the row move of kv_shift_rows, moss_vl_model.cpp:264-291, driven by the

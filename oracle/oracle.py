@@ -202,6 +202,43 @@ def soft_max_row(x, mask=None, scale: float = 1.0) -> np.ndarray:
     return y
 
 
+def _kv_heads_f64(cache, n_kv_head: int, head_dim: int, n_keys: int) -> np.ndarray:
+    """An f16 cache's first n_keys rows as float64 [S, NKV, HD] (exact)."""
+    rows = np.ascontiguousarray(cache[:n_keys]).view(np.uint8)
+    h = rows[:, : n_kv_head * head_dim * 2].copy().view(np.float16)
+    return h.astype(np.float64).reshape(n_keys, n_kv_head, head_dim)
+
+
+def mul_mat_kq(k, q, n_kv_head: int, head_dim: int, n_keys: int) -> np.ndarray:
+    """kq = ggml_mul_mat(kf, qf) of the soft_max fallback (gemma4_model.cpp:685): the raw scores
+    kq[h, t, s] = sum_e k[s, h // (NH // NKV), e] * q[t, h, e] -- ggml broadcasts src0's third
+    dimension over src1's.  q (f32 [T, NH, HD]) is rounded to f16 first, as ggml converts src1 to
+    the vec-dot type of an f16 src0; the sum is taken in float64.  k: f16 cache bytes [rows,
+    row_bytes].  Returns f32 [NH, T, S] (ggml's [S, T, NH])."""
+    kf = _kv_heads_f64(k, n_kv_head, head_dim, n_keys)
+    qf = np.asarray(q, np.float32).astype(np.float16).astype(np.float64)
+    T, NH, HD = qf.shape
+    g = NH // n_kv_head
+    out = np.empty((NH, T, n_keys), np.float64)
+    for h in range(NH):
+        out[h] = qf[:, h, :] @ kf[:, h // g, :].T
+    return out.astype(np.float32)
+
+
+def mul_mat_kqv(v, kq, n_kv_head: int, head_dim: int, n_keys: int) -> np.ndarray:
+    """kqv = ggml_mul_mat(ggml_cont(ggml_transpose(vf)), kq) (gemma4_model.cpp:689-690), then the
+    permute to [HD, NH, T] (:691): out[t, h, e] = sum_s v[s, h // (NH // NKV), e] * kq[h, t, s], in
+    float64.  v: f16 cache bytes; kq f32 [NH, T, S].  Returns f32 [T, NH, HD]."""
+    vf = _kv_heads_f64(v, n_kv_head, head_dim, n_keys)
+    p = np.asarray(kq, np.float64)
+    NH, T, S = p.shape
+    g = NH // n_kv_head
+    out = np.empty((T, NH, head_dim), np.float64)
+    for h in range(NH):
+        out[:, h, :] = p[h] @ vf[:, h // g, :]
+    return out.astype(np.float32)
+
+
 # ----------------------------------------------------------------- q/k norm + rotary embedding
 ROPE_NONE, ROPE_NEOX, ROPE_IMROPE = 0, 2, 40
 

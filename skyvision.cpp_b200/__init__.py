@@ -113,6 +113,9 @@ def lib() -> ctypes.CDLL:
         "sv_attn": (I, [P, I, P, I, I, I, I, F, P, P]),
         "sv_attn_window": (I, [P, I, P, I, I, I, P, P, P, I, F, P, P]),
         "sv_soft_max_ext": (I, [P, I64, I64, SZ, P, I64, SZ, F, P, SZ, P]),
+        "sv_mul_mat_kq": (I, [P, SZ, I, I, I, P, I, SZ, SZ, I, I, P, P]),
+        "sv_mul_mat_kqv_workspace": (SZ, [I, I, I, I, I]),
+        "sv_mul_mat_kqv": (I, [P, SZ, I, I, I, P, SZ, SZ, I, I, P, SZ, SZ, P, SZ, P]),
         "sv_kv_compact": (I, [P, ctypes.POINTER(_Seg), I, I, ctypes.POINTER(I), P]),
         "sv_can_splice": (I, [P, I64, I64, P, I64, ctypes.POINTER(I64)]),
         "sv_session_create": (I, [P, I, I, I, ctypes.POINTER(P)]),
@@ -467,6 +470,44 @@ def soft_max_ext(x, mask=None, scale: float = 1.0, out=None, stream=None):
 
 
 # =================================================================== session
+def mul_mat_kq(k, q, n_kv_head: int, head_dim: int, n_keys: int, out=None, stream=None):
+    """ggml_mul_mat(kf, qf) of the soft_max fallback: k is the cache (rows of n_kv_head*head_dim f16,
+    any row stride), q [T, NH, HD] f16/f32 (the view's t and h strides are taken from the tensor);
+    returns the f32 scores [NH, T, S] (ggml's [S, T, NH])."""
+    import torch
+    T, NH, HD = q.shape
+    assert HD == head_dim
+    if out is None:
+        out = torch.empty((NH, T, n_keys), dtype=torch.float32, device=q.device)
+    qt = TYPE_F32 if q.dtype == torch.float32 else TYPE_F16
+    es = q.element_size()
+    _check("sv_mul_mat_kq", lib().sv_mul_mat_kq(_ptr(k), k.stride(0) * k.element_size(), n_kv_head, head_dim, n_keys,
+                                                _ptr(q), qt, q.stride(0) * es, q.stride(1) * es, T, NH, _ptr(out),
+                                                _stream(stream)))
+    return out
+
+
+def mul_mat_kqv(v, kq, n_kv_head: int, head_dim: int, n_keys: int, out=None, stream=None, workspace=True):
+    """ggml_mul_mat(ggml_cont(ggml_transpose(vf)), kq) + permute: v the cache, kq f32 [NH, T, S] (any
+    t / h strides); returns f32 [T, NH, HD] (the [HD, NH, T] layout the fallback reshapes)."""
+    import torch
+    NH, T, S = kq.shape
+    assert S == n_keys
+    if out is None:
+        out = torch.empty((T, NH, head_dim), dtype=torch.float32, device=kq.device)
+    ws = None
+    wsb = 0
+    if workspace:
+        wsb = lib().sv_mul_mat_kqv_workspace(n_kv_head, head_dim, n_keys, T, NH)
+        if wsb:
+            ws = torch.empty(wsb, dtype=torch.uint8, device=kq.device)
+    _check("sv_mul_mat_kqv", lib().sv_mul_mat_kqv(_ptr(v), v.stride(0) * v.element_size(), n_kv_head, head_dim,
+                                                  n_keys, _ptr(kq), kq.stride(1) * 4, kq.stride(0) * 4, T, NH,
+                                                  _ptr(out), out.stride(0) * 4, out.stride(1) * 4,
+                                                  _ptr(ws) if ws is not None else None, wsb, _stream(stream)))
+    return out
+
+
 def can_splice(cached_ids, n_past: int, ids) -> int:
     """Returns the number of cached rows to skip (0 = no splice)."""
     import numpy as np
