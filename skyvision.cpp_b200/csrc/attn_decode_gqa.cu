@@ -75,7 +75,12 @@ struct GqaCfg {
     static constexpr int PUSH_ML = 16 * ROWS_MAX * HD * 4;
     static_assert(PUSH_ML + 16 * ROWS_MAX * 8 <= RING_B, "merge slots must fit in the stage ring");
     static constexpr int BAR_OFF = RING_B;
-    static constexpr int SMEM = BAR_OFF + (2 * STAGES + 1) * 8 + 16;   // + abort and last-split flags
+    // the launch's query rows of this kv head as f16, staged once per CTA (rows past R are zero);
+    // the row pitch is padded by 16 bytes so the fragment reads of the 8 rows hit distinct banks
+    static constexpr int QPITCH = HD * 2 + 16;
+    static constexpr int Q_OFF = align_up(BAR_OFF + (2 * STAGES + 1) * 8 + 16, 128);   // after the barriers, flags
+    static_assert(Q_OFF % 16 == 0 && QPITCH % 16 == 0, "16-byte stores into the query rows");
+    static constexpr int SMEM = Q_OFF + kRows * QPITCH;
     static_assert(SMEM + 1024 <= 227 * 1024, "shared memory budget");
 };
 
@@ -310,21 +315,22 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
             prefetch_l2(a.q + (size_t)qi * a.q_nb_t + (size_t)(kvh * a.G + g) * a.q_nb_h + (i % lines) * 128);
         }
         if (lane == 0) {
-            // the split's last visible key, from a possibly stale n_past (a hint for the prefetch extent only)
-            int hint = a.causal_base;
-            if (a.causal_base_dev) hint = *reinterpret_cast<const volatile int*>(a.causal_base_dev);
-            const int pf_hi = a.mask_mode == SV_MASK_CAUSAL ? min(kmax, hint + nq + 1) : kmax;
-            const int nt_pf = pf_hi > ks0 ? (pf_hi - ks0 + kBK - 1) / kBK : 0;
             int j0 = 0;
             if (a.n_new > 0 && a.ring_prefill) {
                 // the kernel appends the step's rows itself and the launch before it wrote no cache rows
                 // while letting this one start early: the rows it reads are complete (the appended ones
-                // are patched in below), so the ring can fill now
+                // are patched in below), so the ring can fill now -- first of all, before the n_past
+                // hint below is read (a global load whose latency would hold these copies back)
                 const int nt_max = kmax > ks0 ? (kmax - ks0 + kBK - 1) / kBK : 0;
                 prefetched = min(nt_max, C::STAGES);
                 for (int j = 0; j < prefetched; j++) issue(j, a.row_base + ks0 + j * kBK);
                 j0 = prefetched;
             }
+            // the split's last visible key, from a possibly stale n_past (a hint for the prefetch extent only)
+            int hint = a.causal_base;
+            if (a.causal_base_dev) hint = *reinterpret_cast<const volatile int*>(a.causal_base_dev);
+            const int pf_hi = a.mask_mode == SV_MASK_CAUSAL ? min(kmax, hint + nq + 1) : kmax;
+            const int nt_pf = pf_hi > ks0 ? (pf_hi - ks0 + kBK - 1) / kBK : 0;
             // a few tiles past the ring only: long splits stream the rest (an L2 prefetch of a whole
             // long context would evict itself before use)
             const int pf_end = min(nt_pf, C::STAGES + kL2Ahead);
@@ -364,18 +370,43 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         __syncwarp();
         asm volatile("barrier.sync 1, %0;" ::"n"(kCThreads) : "memory");
     }
-    // consumers: the query rows first (nothing below waits on them until the first tile)
+    // consumers: the query rows first (nothing below waits on them until the first tile).  They are
+    // staged in shared memory with 16-byte loads spread over the consumer threads -- R rows of HD f16
+    // are a few dozen requests, where per-thread fragment loads (16 scattered 4-byte words per
+    // thread) put ~1000 sector requests per CTA into the memory system right after the dependency --
+    // and each thread then reads its fragments from there.
     const int gq = lane >> 2, tq = lane & 3;     // fragment row / column-pair index
     const int q_es = a.q_type == SV_TYPE_F32 ? 4 : 2;
     // Q^T as B fragments: rows k = head-dim, column n = query row gq
     uint32_t qb[HD / 16][2];
     if (warp < kCWarps) {
-        const bool valid = gq < R;
-        const uint8_t* qrow = nullptr;
-        if (valid) {
-            const int qi = gq / a.G, g = gq % a.G;
-            qrow = a.q + (size_t)qi * a.q_nb_t + (size_t)(kvh * a.G + g) * a.q_nb_h;
+        uint8_t* qs = smem + C::Q_OFF;
+        for (int i = threadIdx.x; i < kRows * (HD / 8); i += kCThreads) {
+            const int r = i / (HD / 8), e = (i % (HD / 8)) * 8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r < R) {
+                const uint8_t* src = a.q + (size_t)(r / a.G) * a.q_nb_t + (size_t)(kvh * a.G + r % a.G) * a.q_nb_h +
+                                     (size_t)e * q_es;
+                if (a.q_type == SV_TYPE_F32) {
+                    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                        const float4 f0 = *reinterpret_cast<const float4*>(src);
+                        const float4 f1 = *reinterpret_cast<const float4*>(src + 16);
+                        v = make_uint4(pack_h2(f0.x, f0.y), pack_h2(f0.z, f0.w), pack_h2(f1.x, f1.y),
+                                       pack_h2(f1.z, f1.w));
+                    } else {
+                        const float* f = reinterpret_cast<const float*>(src);
+                        v = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]), pack_h2(f[6], f[7]));
+                    }
+                } else if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                    v = *reinterpret_cast<const uint4*>(src);
+                } else {
+                    const uint32_t* w = reinterpret_cast<const uint32_t*>(src);
+                    v = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            *reinterpret_cast<uint4*>(qs + r * C::QPITCH + e * 2) = v;
         }
+        consumer_sync();
 #pragma unroll
         for (int kk = 0; kk < HD / 16; kk++) {
 #pragma unroll
@@ -383,16 +414,7 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 // q8_0: thread tq's fragment columns are the 4 consecutive elements at 4*tq of the
                 // k-step (in K and Q alike, so the dot products are unchanged)
                 const int e = C::Q8 ? kk * 16 + 4 * tq + 2 * h : kk * 16 + h * 8 + 2 * tq;
-                uint32_t v = 0;
-                if (valid) {
-                    if (a.q_type == SV_TYPE_F32) {
-                        const float2 f = *reinterpret_cast<const float2*>(qrow + (size_t)e * q_es);
-                        v = pack_h2(f.x, f.y);
-                    } else {
-                        v = *reinterpret_cast<const uint32_t*>(qrow + (size_t)e * q_es);
-                    }
-                }
-                qb[kk][h] = v;
+                qb[kk][h] = *reinterpret_cast<const uint32_t*>(qs + gq * C::QPITCH + e * 2);
             }
         }
     }
