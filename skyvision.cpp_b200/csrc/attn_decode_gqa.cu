@@ -888,8 +888,10 @@ cudaError_t launch_gqa_t(const AttnArgs& a, const CUtensorMap* tk, const CUtenso
     // a cluster merge adds one merger CTA per kv head (cluster = splits + 1)
     const int nx = a.cluster_merge ? a.n_splits + 1 : a.n_splits;
     dim3 grid((unsigned)nx, (unsigned)a.NKV, 1u);
-    return launch_pdl_cluster(fa_decode_gqa_kernel<HD, KVT, kPeer>, grid, dim3(kThreads), (size_t)GqaCfg<HD, KVT>::SMEM + 1024, st,
-                              a.cluster_merge ? nx : 1, *tk, *tv, a);
+    // load-balancing cluster placement: measured 6.44 -> 6.29 us per layer on config 2 (36-layer graph;
+    // the spread policy measured the same as the default)
+    return launch_pdl_cluster_ex(fa_decode_gqa_kernel<HD, KVT, kPeer>, grid, dim3(kThreads),
+                                 (size_t)GqaCfg<HD, KVT>::SMEM + 1024, st, a.cluster_merge ? nx : 1, true, *tk, *tv, a);
 }
 
 template <int HD, int KVT>

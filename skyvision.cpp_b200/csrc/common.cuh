@@ -57,16 +57,17 @@ inline bool pdl_enabled() {
 }
 
 // Launch with programmatic stream serialization and, when cluster_x > 1, thread-block
-// clusters of cluster_x CTAs along x.
+// clusters of cluster_x CTAs along x.  `balance`: ask the block scheduler for its load-balancing
+// cluster placement (cudaClusterSchedulingPolicyLoadBalancing) instead of the default one.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                               int cluster_x, Args&&... args) {
+cudaError_t launch_pdl_cluster_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                  int cluster_x, bool balance, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     int n = 0;
     if (pdl_enabled()) {
         attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -79,10 +80,21 @@ cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, 
         attr[n].val.clusterDim.y = 1;
         attr[n].val.clusterDim.z = 1;
         n++;
+        if (balance) {
+            attr[n].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+            attr[n].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicyLoadBalancing;
+            n++;
+        }
     }
     cfg.attrs = attr;
     cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               int cluster_x, Args&&... args) {
+    return launch_pdl_cluster_ex(kernel, grid, block, smem, st, cluster_x, false, std::forward<Args>(args)...);
 }
 
 template <typename... KArgs, typename... Args>
