@@ -46,6 +46,7 @@ constexpr int kCThreads = kCWarps * 32;
 constexpr int kThreads = kCThreads + 32;   // + one TMA producer warp
 constexpr int kRows = 8;                   // query rows per kv head (N of the MMA)
 constexpr int kL2Ahead = 4;                // K/V tiles past the ring prefetched into L2 before the wait
+constexpr int kMergeGroup = 16;            // partials one CTA merges at most (ticket merge, two levels beyond)
 
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
@@ -741,8 +742,12 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 
     if (!a.cluster_merge) {
         // ---- split-K without a cluster (many splits: few kv heads over a long context): every
-        // split publishes its partial to the workspace, and the last CTA of the kv head (atomic
-        // ticket, no spinning) merges all partials and resets the ticket.
+        // split publishes its partial to the workspace.  Up to kMergeGroup splits, the last CTA of the
+        // kv head (atomic ticket, no spinning) merges all partials.  With more splits, and ticket room
+        // for the groups (merge_levels = 2), the merge has two levels, so no CTA reads more than
+        // kMergeGroup partials (a 228-partial merge by one CTA took ~25 us): the last split of each group of
+        // kMergeGroup merges the group into the slot of the group's first split, and the last group
+        // merger of the kv head merges the groups.  Every last CTA resets the ticket it took.
         volatile int* last = flag + 1;
         const int ns = a.n_splits;
         const size_t pbase = ((size_t)kvh * ns + split) * 16;   // 16-row partial slots per split
@@ -764,76 +769,118 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
             *reinterpret_cast<float4*>(&a.ws_o[(pbase + r) * HD + c]) = acc;
             if (c == 0) *reinterpret_cast<float2*>(&a.ws_ml[(pbase + r) * 2]) = make_float2(M, L);
         }
-        __threadfence();
-        consumer_sync();
-        if (tid == 0) *last = atomicAdd(&a.tickets[kvh], 1) == ns - 1;
-        consumer_sync();
-        if (!*last) return;
-        __threadfence();
-        // n_g (row, 4-column) groups over the 256 consumer threads: P threads per group, each merging
-        // every P-th split online (running max, rescaled sum) with the (m, l) pairs and partial rows
-        // of 16 splits loaded together, so the whole merge is a few L2 round trips; then the P
-        // partial merges meet in shared memory.
         const size_t tbase = (size_t)kvh * ns * 16;
+        // n_g (row, 4-column) groups over the 256 consumer threads: P threads per group, each merging
+        // every P-th of `cnt` partials (slot of partial u: split first + u * stride) online (running
+        // max, rescaled sum) with the (m, l) pairs and partial rows of 16 partials loaded together, so
+        // the merge is a few L2 round trips; then the P partial merges meet in shared memory.  Threads
+        // gi < n_g return the merged (M, L, unnormalised O) of their group.
         const int P = max(1, kCThreads / n_g);
         float4* part_o = reinterpret_cast<float4*>(smem);                   // [P][n_g]
         float2* part_ml = reinterpret_cast<float2*>(smem + (size_t)P * n_g * sizeof(float4));
-        if (tid < P * n_g) {
-            const int gi = tid % n_g, sub = tid / n_g;
-            const int r = gi / G4, c = (gi % G4) * 4;
-            float M = -INFINITY, L = 0.0f;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sp0 = sub; sp0 < ns; sp0 += 16 * P) {
-                float2 ml[16];
-                float4 v[16];
+        auto merge_partials = [&](int first, int stride, int cnt, float& Mo, float& Lo, float4& Ao) {
+            if (tid < P * n_g) {
+                const int gi = tid % n_g, sub = tid / n_g;
+                const int r = gi / G4, c = (gi % G4) * 4;
+                float M = -INFINITY, L = 0.0f;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int u0 = sub; u0 < cnt; u0 += 16 * P) {
+                    float2 ml[16];
+                    float4 v[16];
 #pragma unroll
-                for (int u = 0; u < 16; u++) {
-                    const int sp = sp0 + u * P;
-                    if (sp < ns) {
-                        const size_t slot = tbase + (size_t)sp * 16 + r;
-                        ml[u] = __ldcg(reinterpret_cast<const float2*>(&a.ws_ml[slot * 2]));
-                        v[u] = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[slot * HD + c]));
-                    } else {
-                        ml[u] = make_float2(-INFINITY, 0.0f);
+                    for (int uu = 0; uu < 16; uu++) {
+                        const int u = u0 + uu * P;
+                        if (u < cnt) {
+                            const size_t slot = tbase + (size_t)(first + u * stride) * 16 + r;
+                            ml[uu] = __ldcg(reinterpret_cast<const float2*>(&a.ws_ml[slot * 2]));
+                            v[uu] = __ldcg(reinterpret_cast<const float4*>(&a.ws_o[slot * HD + c]));
+                        } else {
+                            ml[uu] = make_float2(-INFINITY, 0.0f);
+                        }
                     }
-                }
-                float mb = M;
+                    float mb = M;
 #pragma unroll
-                for (int u = 0; u < 16; u++) mb = fmaxf(mb, ml[u].x);
-                if (mb == -INFINITY) continue;
-                const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
-                L *= sc;
-                acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+                    for (int uu = 0; uu < 16; uu++) mb = fmaxf(mb, ml[uu].x);
+                    if (mb == -INFINITY) continue;
+                    const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
+                    L *= sc;
+                    acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
 #pragma unroll
-                for (int u = 0; u < 16; u++) {
-                    if (ml[u].x != -INFINITY) {
-                        const float w = fast_exp2(ml[u].x - mb);
-                        L += ml[u].y * w;
-                        acc.x += v[u].x * w; acc.y += v[u].y * w; acc.z += v[u].z * w; acc.w += v[u].w * w;
+                    for (int uu = 0; uu < 16; uu++) {
+                        if (ml[uu].x != -INFINITY) {
+                            const float w = fast_exp2(ml[uu].x - mb);
+                            L += ml[uu].y * w;
+                            acc.x += v[uu].x * w; acc.y += v[uu].y * w; acc.z += v[uu].z * w; acc.w += v[uu].w * w;
+                        }
                     }
+                    M = mb;
                 }
-                M = mb;
+                part_o[sub * n_g + gi] = acc;
+                part_ml[sub * n_g + gi] = make_float2(M, L);
             }
-            part_o[sub * n_g + gi] = acc;
-            part_ml[sub * n_g + gi] = make_float2(M, L);
+            consumer_sync();
+            if (tid < n_g) {
+                const int gi = tid;
+                float M = -INFINITY;
+                for (int sub = 0; sub < P; sub++) M = fmaxf(M, part_ml[sub * n_g + gi].x);
+                float L = 0.0f;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int sub = 0; sub < P; sub++) {
+                    const float2 ml = part_ml[sub * n_g + gi];
+                    if (ml.x == -INFINITY) continue;
+                    const float w = fast_exp2(ml.x - M);
+                    const float4 v = part_o[sub * n_g + gi];
+                    L += ml.y * w;
+                    acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+                }
+                Mo = M;
+                Lo = L;
+                Ao = acc;
+            }
+        };
+        float Mf = -INFINITY, Lf = 0.0f;
+        float4 Af = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int n_grp = (ns + kMergeGroup - 1) / kMergeGroup;
+        if (a.merge_levels == 2 && n_grp > 1) {
+            // ---- level 1: the last split of this group of kMergeGroup merges the group
+            const int grp = split / kMergeGroup, g0 = grp * kMergeGroup, gn = min(kMergeGroup, ns - g0);
+            int* gticket = &a.tickets[a.NKV + kvh * n_grp + grp];
+            __threadfence();
+            consumer_sync();
+            if (tid == 0) *last = atomicAdd(gticket, 1) == gn - 1;
+            consumer_sync();
+            if (!*last) return;
+            __threadfence();
+            merge_partials(g0, 1, gn, Mf, Lf, Af);
+            // the group's partial replaces its first split's, which only this CTA reads
+            if (tid < n_g) {
+                const int r = tid / G4, c = (tid % G4) * 4;
+                const size_t slot = tbase + (size_t)g0 * 16 + r;
+                *reinterpret_cast<float4*>(&a.ws_o[slot * HD + c]) = Af;
+                if (c == 0) *reinterpret_cast<float2*>(&a.ws_ml[slot * 2]) = make_float2(Mf, Lf);
+            }
+            if (tid == 0) *gticket = 0;
+            __threadfence();
+            consumer_sync();   // every thread is done with part_o / part_ml and has published
+            // ---- level 2: the last group merger of the kv head merges the groups
+            if (tid == 0) *last = atomicAdd(&a.tickets[kvh], 1) == n_grp - 1;
+            consumer_sync();
+            if (!*last) return;
+            __threadfence();
+            merge_partials(0, kMergeGroup, n_grp, Mf, Lf, Af);
+        } else {
+            __threadfence();
+            consumer_sync();
+            if (tid == 0) *last = atomicAdd(&a.tickets[kvh], 1) == ns - 1;
+            consumer_sync();
+            if (!*last) return;
+            __threadfence();
+            merge_partials(0, 1, ns, Mf, Lf, Af);
         }
-        consumer_sync();
-        for (int gi = tid; gi < n_g; gi += kCThreads) {
-            const int r = gi / G4, c = (gi % G4) * 4;
-            float M = -INFINITY;
-            for (int sub = 0; sub < P; sub++) M = fmaxf(M, part_ml[sub * n_g + gi].x);
-            float L = 0.0f;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sub = 0; sub < P; sub++) {
-                const float2 ml = part_ml[sub * n_g + gi];
-                if (ml.x == -INFINITY) continue;
-                const float w = fast_exp2(ml.x - M);
-                const float4 v = part_o[sub * n_g + gi];
-                L += ml.y * w;
-                acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
-            }
-            const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-            store_out4<kPeer>(a, kvh, r, c, make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
+        if (tid < n_g) {
+            const int r = tid / G4, c = (tid % G4) * 4;
+            const float inv = Lf > 0.0f ? 1.0f / Lf : 0.0f;
+            store_out4<kPeer>(a, kvh, r, c, make_float4(Af.x * inv, Af.y * inv, Af.z * inv, Af.w * inv));
         }
         if (tid == 0) a.tickets[kvh] = 0;
         signal_peers<kPeer>(a, 1, kCThreads);

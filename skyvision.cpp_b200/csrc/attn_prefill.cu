@@ -14,25 +14,33 @@
 // kv head, so every K/V tile feeds all heads of the GQA group, and with NQT = 2 each K/V tile
 // read from L2 feeds 256 rows.  Warp roles ((4*NQT + 3) warps):
 //   softmax warps (4 per query tile; warp w reads TMEM lane quarter w % 4, one row per thread):
-//              per 64-key tile read S (64 columns) with tcgen05.ld, apply scale and the causal
-//              predicate, take the row max, write P = exp2(S - m) as f16 over the first 32
+//              per key tile read S (BN columns) with tcgen05.ld, apply scale and the causal
+//              predicate, take the row max, write P = exp2(S - m) as f16 over the first BN/2
 //              columns of the same TMEM buffer (the P.V MMA reads A from TMEM), and, when the
-//              row max grew, rescale the row of O in TMEM after the exponentials (which overlap
-//              the previous tile's P.V).  One exponential in four runs on the FMA pipe
-//              (exp2_fma) to take load off the SFU.
+//              row max grew, rescale the row of O in TMEM after the exponentials.  One
+//              exponential in four runs on the FMA pipe (exp2_fma) to take load off the SFU
+//              (two in four measured slower: the FMA pipe, not the SFU, is the tighter one).
 //   TMA warps  one lane of the first loads the query tiles (a 3D map over [T][NH][HD] whose
 //              {64, G, 128/G} box is one slab of a tile) and streams K tiles, one lane of the second
 //              V tiles, each into its own ring (5 stages at HD 128, 2 at HD 256); a K stage is
 //              refilled as soon as its S has completed, a V stage after its P.V.  The two rings have
 //              a warp each: as two lanes of one warp, a V lane blocked in its slot wait held back the
 //              K lane's loads (~450 cycles of the MMA thread's wait per tile, in-kernel stamps).
-//   MMA warp   (one thread) S double-buffered in TMEM per query tile, so the tensor core computes
-//              S(j+1) while the softmax warps work on S(j):
-//                S  = Q K^T   M=128, N=64 keys, K=HD   (A, B K-major, shared memory)
-//                O += P V     M=128, N=HD,      K=64   (A = P from TMEM, B = V MN-major)
+//   MMA warp   (one thread)
+//                S  = Q K^T   M=128, N=BN keys, K=HD   (A, B K-major, shared memory)
+//                O += P V     M=128, N=HD,      K=BN   (A = P from TMEM, B = V MN-major)
 //              completions reach the other roles through tcgen05.commit on mbarriers (per
 //              parity of the tile index where a role can run a tile ahead).
-// TMEM per query tile: S/P buffers in columns [0, 64) and [64, 128), O in [128, 128 + HD).
+//              BN = 64 (one query tile, HD 256, q8_0 parts): S double-buffered per query tile,
+//              so the tensor core computes S(j+1) while the softmax warps work on S(j).
+//              BN = 128 (two query tiles of an f16 cache at HD 128): one 128-column S buffer per
+//              query tile; S_q(j+1) is issued right after P.V_q(j) (it overwrites P_q(j); the
+//              tensor pipe runs in order), and the query tiles alternate, so the tensor core runs
+//              P.V_1(j), S_1(j+1) while query tile 0's softmax works on S_0(j+1).  N = 128 S MMAs
+//              halve the S instructions per key: the tensor front end takes an N = 64 MMA about
+//              every 84 cycles, barely more than the N = 128 one's ~92 cycles of work.
+// TMEM per query tile: S/P buffers in columns [0, 64) and [64, 128) (BN = 64) or one buffer in
+// [0, 128) (BN = 128), O in [128, 128 + HD).
 // Splits: when the units (query tiles x kv heads) are fewer than the SMs, the key range of a
 // unit is cut into up to 8 splits (one CTA per SM, no clusters, so every SM is usable).  The
 // splits take an arrival ticket; all but the last publish their partial (O, m, l) to the
@@ -40,10 +48,15 @@
 // which never leaves TMEM.
 //
 // Measured (config 2 splice tail, 384 over 4096 cached rows, one B200): 448 TFLOP/s over 36
-// layers; config 4's q8_0 chunks 280 TFLOP/s (algorithmic).  In-kernel clock stamps per 64-key
-// tile (two query tiles): ~3250 cycles a tile, of which the softmax warps compute ~2000 and wait
-// ~1160 for the next S, while the issuing thread blocks ~1340 cycles issuing the tile's 16 N = 64
-// S MMAs.
+// layers with 64-key tiles, 490 with 128-key tiles; config 4's q8_0 chunks ~297 TFLOP/s
+// (algorithmic).  In-kernel clock stamps per 128-key tile (two query tiles): ~4950 cycles a
+// tile.  Per query tile the softmax takes ~2900 (S load 185, max + exponentials ~1780, O rescale
+// and P store ~940) and its P.V + next S MMAs ~1800 (the issuing thread blocks ~92 cycles per
+// N = 128 S MMA and ~130 per P.V MMA), one after the other, so the tensor pipe idles ~30 % of a
+// tile.  Measured and dropped: two threads per row (16 softmax warps: the 19-warp block gets 96
+// registers and spills, 169 TFLOP/s); a two-pass softmax whose TMEM reloads overlap the
+// exponentials (386); a rescale threshold of 2^8 (the dominant weights' f16 rounding then
+// breaks the 2e-3 gate on x8-outlier V rows, even with the row sum taken over rounded weights).
 //
 // Roofline: tensor-bound.  Algorithmic FLOPs per launch = 4 * NH * HD * sum
 // over queries of visible keys (masked keys do not count).
@@ -63,6 +76,11 @@ namespace {
 // (A lazy rescale that lets the running max trail by up to 2^8 saves the O round trips but rounds the
 // dominant weights: with x8 outlier V rows it cost ~1e-3 of max-abs error, measured on the GPU.)
 constexpr float kRescaleLog2 = 0.0f;
+// softmax exponentials per four that run on the FMA pipe (exp2_fma); the rest use the SFU
+#ifndef SVKV_EXP_FMA
+#define SVKV_EXP_FMA 1
+#endif
+constexpr int kExpFma = SVKV_EXP_FMA;
 // P parts on f16 caches (1: P rounded to f16, standard flash-attention precision)
 constexpr int kF16PParts = 1;
 
@@ -86,19 +104,27 @@ __device__ __forceinline__ float exp2_fma(float x) {
 // tiles; NP = 2: every K and V tile arrives as two f16 parts (hi, lo) whose sum is the exact
 // dequantised q8_0 value, and both parts go through the tensor core into the same accumulator.
 // The K and V rings hold single parts ("entries"), so a tile takes NP consecutive entries.
-template <int HD, int NQT, int NP = 1>
+// BN = keys per tile.  BN = 64: S double-buffered per Q tile (two 64-column buffers); BN = 128 (f16,
+// HD 128): one 128-column S buffer per Q tile, and the two Q tiles alternate on the tensor core, so
+// every S MMA is N = 128 (half the S instructions per key of BN = 64).
+template <int HD, int NQT, int NP = 1, int BN_ = 64>
 struct PreCfg {
-    static constexpr int BN = 64;                         // keys per tile
+    static constexpr int BN = BN_;                        // keys per tile
+    static constexpr bool S2 = BN == 64;                  // S double-buffered per Q tile
+
     static constexpr int BOX_ROW = 128;                   // bytes per swizzled row (64 f16)
     static constexpr int QBOX = 128 * BOX_ROW;            // one 64-column slab of a Q tile
     static constexpr int Q_B = (HD / 64) * QBOX;          // one Q tile
     static constexpr int KBOX = BN * BOX_ROW;             // one 64-column slab of a K or V tile
     static constexpr int KV_B = (HD / 64) * KBOX;         // one part of a K (or V) tile: a ring entry
     static constexpr int ENT_FIT = (227 * 1024 - NQT * Q_B - 2048) / KV_B;
-    // f16: up to 5 stages of (K, V); hi + lo parts: the entries that fit, split between K and V
-    static constexpr int NEK = NP == 1 ? (ENT_FIT / 2 > 5 ? 5 : ENT_FIT / 2) : ((ENT_FIT + 1) / 2 > 5 * NP ? 5 * NP : (ENT_FIT + 1) / 2);
-    static constexpr int NEV = NP == 1 ? NEK : (ENT_FIT / 2 > 5 * NP ? 5 * NP : ENT_FIT / 2);
+    // f16: up to 5 stages of (K, V) (BN = 128: the entries that fit, one more for K); hi + lo parts:
+    // the entries that fit, split between K and V
+    static constexpr int NEK = NP == 1 ? (BN == 128 ? (ENT_FIT + 1) / 2 : (ENT_FIT / 2 > 5 ? 5 : ENT_FIT / 2))
+                                       : ((ENT_FIT + 1) / 2 > 5 * NP ? 5 * NP : (ENT_FIT + 1) / 2);
+    static constexpr int NEV = NP == 1 ? (BN == 128 ? ENT_FIT / 2 : NEK) : (ENT_FIT / 2 > 5 * NP ? 5 * NP : ENT_FIT / 2);
     static_assert(NEK >= 2 && NEK >= NP && NEV >= NP && NEV >= 2, "K/V rings need two entries and a whole tile");
+    static_assert(BN == 64 || (BN == 128 && NP == 1), "128-key tiles: f16 caches");
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + NQT * Q_B;
     static constexpr int OFF_V = OFF_K + NEK * KV_B;
@@ -106,7 +132,7 @@ struct PreCfg {
     static constexpr int N_BAR = 2 * NEK + 2 * NEV + 1 + NQT * 6;
     static constexpr int SMEM = OFF_BAR + N_BAR * 8 + 16;
     static_assert(SMEM + 1024 <= 227 * 1024, "shared memory budget");
-    static constexpr int QCOLS = 128 + HD;                // per Q tile: S/P buffers [0, 64) and [64, 128), O after
+    static constexpr int QCOLS = 128 + HD;                // per Q tile: S/P buffer(s) in [0, 128), O after
     static constexpr int TMEM_COLS = NQT * QCOLS <= 256 ? 256 : 512;
     static_assert(NQT * QCOLS <= 512, "TMEM budget");
     static constexpr int SM_WARPS = 4 * NQT;              // softmax warps: one row per thread
@@ -139,12 +165,12 @@ __device__ __forceinline__ void softmax_sync() {
 // tmk/tmv: the f16 cache tensors, or (NP = 2) the hi parts; tmk2/tmv2: the lo parts (NP = 2 only).
 // PL = 2: P goes to the tensor core as f16 hi + lo parts (O += P_hi V + P_lo V_hi), so the weights
 // keep ~22 bits; PL = 1: P rounded to f16.
-template <int HD, int NQT, int NP, int PL>
-__global__ void __launch_bounds__(PreCfg<HD, NQT, NP>::THREADS, 1)
+template <int HD, int NQT, int NP, int PL, int BN>
+__global__ void __launch_bounds__(PreCfg<HD, NQT, NP, BN>::THREADS, 1)
 fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                   const __grid_constant__ CUtensorMap tmk2, const __grid_constant__ CUtensorMap tmv2,
                   const __grid_constant__ CUtensorMap tmq, const __grid_constant__ AttnArgs a) {
-    using C = PreCfg<HD, NQT, NP>;
+    using C = PreCfg<HD, NQT, NP, BN>;
     constexpr int kSoftmaxWarps = C::SM_WARPS;
     constexpr int kTmaWarp = kSoftmaxWarps;   // Q and K producer; then the V producer and the MMA issuer
     extern __shared__ uint8_t smem_raw[];
@@ -231,8 +257,8 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
     if (warp < kSoftmaxWarps) {
         // ============================ softmax warps: one row of one Q tile per thread
         // Q tile qtl = warp / 4, TMEM lane quarter warp % 4 (rows 32*quarter + lane).  Per key tile:
-        // S (64 columns) from TMEM, scale and causal mask, row max, P = exp2(S - m) written back as
-        // f16 over the first 32 columns of the same TMEM buffer (the P.V MMA reads it from there),
+        // S (BN columns) from TMEM, scale and causal mask, row max, P = exp2(S - m) written back as
+        // f16 over the first BN/2 columns of the same TMEM buffer (the P.V MMA reads it from there),
         // and, when the row max grew, O rescaled in TMEM.
         const int qtl = warp >> 2, quarter = warp & 3;
         const bool tile_live = qtl < nqt;
@@ -281,24 +307,30 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
             if (!warp_wait(&sf[i & 1], (i >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
             tc_fence_after();
             const int kb = tile_of(i) * C::BN;           // first key of the tile
-            const uint32_t sbuf = lane_addr + (i & 1) * C::BN;
-            float s[64];
-            tmem_ld32(sbuf, s);
-            tmem_ld32(sbuf + 32, s + 32);
-            tmem_wait_ld();
+            const uint32_t sbuf = lane_addr + (C::S2 ? (i & 1) * C::BN : 0);
             // keys past the row's position (or past kend) are masked; only the last tiles have any
-            if (kb + 63 > qpos || kb + 64 > kend) {
+            const bool edge = kb + C::BN - 1 > qpos || kb + C::BN > kend;
+            float s[C::BN];
 #pragma unroll
-                for (int k = 0; k < 64; k++)
+            for (int cc = 0; cc < C::BN; cc += 32) tmem_ld32(sbuf + cc, s + cc);
+            tmem_wait_ld();
+            if (edge) {
+#pragma unroll
+                for (int k = 0; k < C::BN; k++)
                     if (kb + k > qpos || kb + k >= kend) s[k] = -INFINITY;
             }
-            float m8[8];
+            // ---- the row max over the tile's BN columns
+            float mr = -INFINITY;
 #pragma unroll
-            for (int k = 0; k < 8; k++)
-                m8[k] = fmaxf(fmaxf(fmaxf(s[k], s[k + 8]), fmaxf(s[k + 16], s[k + 24])),
-                              fmaxf(fmaxf(s[k + 32], s[k + 40]), fmaxf(s[k + 48], s[k + 56])));
-            const float mr = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            for (int h = 0; h < C::BN; h += 64) {
+                float m8[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    m8[k] = fmaxf(fmaxf(fmaxf(s[h + k], s[h + k + 8]), fmaxf(s[h + k + 16], s[h + k + 24])),
+                                  fmaxf(fmaxf(s[h + k + 32], s[h + k + 40]), fmaxf(s[h + k + 48], s[h + k + 56])));
+                mr = fmaxf(mr, fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                     fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))));
+            }
             const float mt = mr * c;                     // scale > 0 commutes with max
             float alpha = 1.0f;
             bool resc = false;
@@ -311,44 +343,61 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
             }
             const float mneg = m_use == -INFINITY ? 0.0f : -m_use;
             float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t pk[32];
-            uint32_t pl[PL == 2 ? 32 : 1];
+            // exponentials of 32 keys (register copy sv of their S columns) -> 16 packed f16 P words
+            // (and the P_lo words with PL = 2)
+            auto exp32 = [&](const float* sv, uint32_t* pk, uint32_t* pl) {
 #pragma unroll
-            for (int k = 0; k < 64; k += 4) {
-                // three of every four on the SFU, one on the FMA pipe
-                const float p0 = fast_exp2(fmaf(s[k], c, mneg));
-                const float p1 = fast_exp2(fmaf(s[k + 1], c, mneg));
-                const float p2 = fast_exp2(fmaf(s[k + 2], c, mneg));
-                const float p3 = exp2_fma(fmaf(s[k + 3], c, mneg));
-                sum4[(k >> 2) & 3] += (p0 + p1) + (p2 + p3);
-                const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
-                pk[k >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
-                pk[(k >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
-                if constexpr (PL == 2) {
-                    // p - f16(p) is exact in f32; its f16 rounding leaves ~2^-22 of p
-                    const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
-                    pl[k >> 1] = pack_h2(p0 - f01.x, p1 - f01.y);
-                    pl[(k >> 1) + 1] = pack_h2(p2 - f23.x, p3 - f23.y);
+                for (int k = 0; k < 32; k += 4) {
+                    const float* x = sv + k;   // masked keys are -inf already
+                    // three of every four on the SFU, one on the FMA pipe (kExpFma of four)
+                    const float p0 = fast_exp2(fmaf(x[0], c, mneg));
+                    const float p1 = kExpFma >= 3 ? exp2_fma(fmaf(x[1], c, mneg)) : fast_exp2(fmaf(x[1], c, mneg));
+                    const float p2 = kExpFma >= 2 ? exp2_fma(fmaf(x[2], c, mneg)) : fast_exp2(fmaf(x[2], c, mneg));
+                    const float p3 = exp2_fma(fmaf(x[3], c, mneg));
+                    const __half2 h01 = __floats2half2_rn(p0, p1), h23 = __floats2half2_rn(p2, p3);
+                    sum4[(k >> 2) & 3] += (p0 + p1) + (p2 + p3);
+                    pk[k >> 1] = *reinterpret_cast<const uint32_t*>(&h01);
+                    pk[(k >> 1) + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+                    if constexpr (PL == 2) {
+                        // p - f16(p) is exact in f32; its f16 rounding leaves ~2^-22 of p
+                        const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+                        pl[k >> 1] = pack_h2(p0 - f01.x, p1 - f01.y);
+                        pl[(k >> 1) + 1] = pack_h2(p2 - f23.x, p3 - f23.y);
+                    }
                 }
-            }
-            // the exponentials above overlapped P.V(i-1); O is stable once it has completed
-            if (__any_sync(0xffffffffu, resc)) {
-                if (!warp_wait(&od[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
-                tc_fence_after();
+            };
+            const bool any_resc = __any_sync(0xffffffffu, resc);
+            {
+                uint32_t pk[C::BN / 2];
+                uint32_t pl[PL == 2 ? C::BN / 2 : 1];
+#pragma unroll
+                for (int cc = 0; cc < C::BN; cc += 32)
+                    exp32(s + cc, pk + cc / 2, PL == 2 ? pl + cc / 2 : pl);
+                // the exponentials above overlapped P.V(i-1) (64-key tiles; with 128-key tiles it
+                // completed before S(i)); O is stable once it has completed
+                if (any_resc) {
+                    if (!warp_wait(&od[(i - 1) & 1], ((i - 1) >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
+                    tc_fence_after();
+                    // 64 columns per TMEM round trip (the S registers are free by now)
 #pragma unroll 1
-                for (int cc = 0; cc < HD; cc += 32) {
-                    float o[32];
-                    tmem_ld32(lane_addr + 128 + cc, o);
-                    tmem_wait_ld();
+                    for (int cc = 0; cc < HD; cc += 64) {
+                        float o[64];
+                        tmem_ld32(lane_addr + 128 + cc, o);
+                        tmem_ld32(lane_addr + 128 + cc + 32, o + 32);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int k = 0; k < 32; k++) o[k] *= alpha;
-                    tmem_st32(lane_addr + 128 + cc, o);
+                        for (int k = 0; k < 64; k++) o[k] *= alpha;
+                        tmem_st32(lane_addr + 128 + cc, o);
+                        tmem_st32(lane_addr + 128 + cc + 32, o + 32);
+                    }
                 }
+                // P over the first BN/2 columns of this tile's S buffer (the S MMA that next writes the
+                // buffer, S(i+2) or with one buffer S(i+1), is issued only after P.V(i), and the tensor
+                // pipe runs in order)
+#pragma unroll
+                for (int cc = 0; cc < C::BN / 2; cc += 32) tmem_st32(sbuf + cc, reinterpret_cast<const float*>(pk + cc));
+                if constexpr (PL == 2) tmem_st32(sbuf + 32, reinterpret_cast<const float*>(pl));   // P_lo after P_hi
             }
-            // P over the first 32 columns of this tile's S buffer (S(i+2) reuses the buffer only
-            // after P.V(i) has been issued, and the tensor pipe runs in order)
-            tmem_st32(sbuf, reinterpret_cast<const float*>(pk));
-            if constexpr (PL == 2) tmem_st32(sbuf + 32, reinterpret_cast<const float*>(pl));   // P_lo after P_hi
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             tmem_wait_st();
             tc_fence_before();
@@ -527,7 +576,11 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
                 mbar_arrive_expect_tx(&fullx[s], C::KV_B);
                 const int y = a.row_base + tile_of(e / NP) * C::BN;
 #pragma unroll
-                for (int b = 0; b < HD / 64; b++) tma_load_2d(dst + b * C::KBOX, tm, kvh * HD + b * 64, y, &fullx[s]);
+                for (int b = 0; b < HD / 64; b++)
+#pragma unroll
+                    for (int h = 0; h < C::BN / 64; h++)   // the tensor map's box is 64 rows
+                        tma_load_2d(dst + b * C::KBOX + h * 64 * C::BOX_ROW, tm, kvh * HD + b * 64, y + h * 64,
+                                    &fullx[s]);
                 issued = e + 1;
             }
             for (int e = max(0, issued - NE); e < issued; e++)
@@ -546,70 +599,104 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
             const uint32_t q_lo = desc_lo(smem_u32(smem + C::OFF_Q), 16);
             const uint32_t k_lo = desc_lo(smem_u32(smem + C::OFF_K), 16);
             const uint32_t v_lo = desc_lo(smem_u32(smem + C::OFF_V), C::KBOX);
-            // S(i) = Q K(i)^T into buffer i & 1 of every live Q tile, summed over the NP parts of K(i)
-            auto issue_s = [&](int i) -> bool {
+            // S(i) = Q K(i)^T into Q tile q's S buffer (buffer i & 1 when double-buffered), summed over the
+            // NP parts of K(i); the K entries of tile i must have landed (wait_k)
+            auto wait_k = [&](int i) -> bool {
                 for (int p = 0; p < NP; p++) {
                     const int e = i * NP + p;
                     if (!wait_or_abort(&full_k[e % C::NEK], (e / C::NEK) & 1, a.err, abort_flag)) return false;
                 }
                 tc_fence_after();
+                return true;
+            };
+            auto mma_s = [&](int i, int q) {
                 uint32_t kd[NP];
 #pragma unroll
                 for (int p = 0; p < NP; p++) kd[p] = k_lo + (uint32_t)(((i * NP + p) % C::NEK) * (C::KV_B >> 4));
+                const uint32_t d_tmem = tmem + q * C::QCOLS + (C::S2 ? (i & 1) * C::BN : 0);
 #pragma unroll
-                for (int q = 0; q < NQT; q++) {
-                    if (q >= nqt) break;
-                    const uint32_t d_tmem = tmem + q * C::QCOLS + (i & 1) * C::BN;
+                for (int p = 0; p < NP; p++) {
 #pragma unroll
-                    for (int p = 0; p < NP; p++) {
-#pragma unroll
-                        for (int kk = 0; kk < HD / 16; kk++) {
-                            const uint32_t a_off = (uint32_t)((q * C::Q_B + (kk / 4) * C::QBOX + (kk % 4) * 32) >> 4);
-                            const uint32_t b_off = (uint32_t)(((kk / 4) * C::KBOX + (kk % 4) * 32) >> 4);
-                            umma_f16_w(d_tmem, q_lo + a_off, kd[p] + b_off, hi, idesc_s,
-                                       (kk > 0 || p > 0) ? 1u : 0u);
-                        }
+                    for (int kk = 0; kk < HD / 16; kk++) {
+                        const uint32_t a_off = (uint32_t)((q * C::Q_B + (kk / 4) * C::QBOX + (kk % 4) * 32) >> 4);
+                        const uint32_t b_off = (uint32_t)(((kk / 4) * C::KBOX + (kk % 4) * 32) >> 4);
+                        umma_f16_w(d_tmem, q_lo + a_off, kd[p] + b_off, hi, idesc_s, (kk > 0 || p > 0) ? 1u : 0u);
                     }
-                    umma_commit(&s_full[2 * q + (i & 1)]);
                 }
-                // the K entries are free once every S(i) has completed
-                for (int p = 0; p < NP; p++) umma_commit(&empty_k[(i * NP + p) % C::NEK]);
-                return true;
+                umma_commit(&s_full[2 * q + (i & 1)]);
             };
-            bool ok = wait_or_abort(q_full, 0, a.err, abort_flag);
-            if (ok) ok = issue_s(0);
-            for (int i = 0; ok && i < n; i++) {
-                // S(i+1) overlaps the softmax of tile i (its buffer held S(i-1), whose P.V was issued)
-                if (i + 1 < n && !issue_s(i + 1)) break;
-                for (int p = 0; p < NP && ok; p++) {
-                    const int e = i * NP + p;
-                    ok = wait_or_abort(&full_v[e % C::NEV], (e / C::NEV) & 1, a.err, abort_flag);
-                }
+            // the K entries of tile i are free once every S(i) has completed
+            auto release_k = [&](int i) {
+                for (int p = 0; p < NP; p++) umma_commit(&empty_k[(i * NP + p) % C::NEK]);
+            };
+            // O += P(i) V(i) for Q tile q, once its softmax warps have written P(i)
+            auto mma_pv = [&](int i, int q) -> bool {
+                if (!wait_or_abort(&p_full[2 * q + (i & 1)], (i >> 1) & 1, a.err, abort_flag)) return false;
+                tc_fence_after();
                 uint32_t vd[NP];
 #pragma unroll
                 for (int p = 0; p < NP; p++) vd[p] = v_lo + (uint32_t)(((i * NP + p) % C::NEV) * (C::KV_B >> 4));
+                // f16 P: 8 columns per 16 keys; P_lo (PL = 2) in the next 32 columns
+                const uint32_t p_tmem = tmem + q * C::QCOLS + (C::S2 ? (i & 1) * C::BN : 0);
+                const uint32_t o_tmem = tmem + q * C::QCOLS + 128;
 #pragma unroll
-                for (int q = 0; q < NQT; q++) {
-                    if (q >= nqt || !ok) break;
-                    if (!wait_or_abort(&p_full[2 * q + (i & 1)], (i >> 1) & 1, a.err, abort_flag)) { ok = false; break; }
-                    tc_fence_after();
-                    // f16 P: 8 columns per 16 keys; P_lo (PL = 2) in the next 32 columns
-                    const uint32_t p_tmem = tmem + q * C::QCOLS + (i & 1) * C::BN;
-                    const uint32_t o_tmem = tmem + q * C::QCOLS + 128;
+                for (int p = 0; p < NP; p++) {
 #pragma unroll
-                    for (int p = 0; p < NP; p++) {
+                    for (int pp = 0; pp < (p == 0 ? PL : 1); pp++) {   // P_lo meets V's first part only
 #pragma unroll
-                        for (int pp = 0; pp < (p == 0 ? PL : 1); pp++) {   // P_lo meets V's first part only
-#pragma unroll
-                            for (int kk = 0; kk < C::BN / 16; kk++)
-                                umma_f16_ts_w(o_tmem, p_tmem + pp * 32 + kk * 8, vd[p] + (uint32_t)(kk * 16 * 128 >> 4), hi,
-                                              idesc_o, (i > 0 || p > 0 || pp > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < C::BN / 16; kk++)
+                            umma_f16_ts_w(o_tmem, p_tmem + pp * 32 + kk * 8, vd[p] + (uint32_t)(kk * 16 * 128 >> 4), hi,
+                                          idesc_o, (i > 0 || p > 0 || pp > 0 || kk > 0) ? 1u : 0u);
+                    }
+                }
+                umma_commit(&o_done[2 * q + (i & 1)]);
+                return true;
+            };
+            auto wait_v = [&](int i) -> bool {
+                for (int p = 0; p < NP; p++) {
+                    const int e = i * NP + p;
+                    if (!wait_or_abort(&full_v[e % C::NEV], (e / C::NEV) & 1, a.err, abort_flag)) return false;
+                }
+                return true;
+            };
+            auto release_v = [&](int i) {
+                for (int p = 0; p < NP; p++) umma_commit(&empty_v[(i * NP + p) % C::NEV]);
+            };
+            bool ok = wait_or_abort(q_full, 0, a.err, abort_flag) && wait_k(0);
+            if (ok) {
+                for (int q = 0; q < nqt; q++) mma_s(0, q);
+                release_k(0);
+            }
+            if constexpr (C::S2) {
+                for (int i = 0; ok && i < n; i++) {
+                    // S(i+1) overlaps the softmax of tile i (its buffer held S(i-1), whose P.V was issued)
+                    if (i + 1 < n) {
+                        if (!wait_k(i + 1)) break;
+                        for (int q = 0; q < nqt; q++) mma_s(i + 1, q);
+                        release_k(i + 1);
+                    }
+                    ok = wait_v(i);
+                    for (int q = 0; q < nqt && ok; q++) ok = mma_pv(i, q);
+                    if (!ok) break;
+                    release_v(i);
+                }
+            } else {
+                // one S buffer per Q tile: S_q(i+1) follows P.V_q(i) (it overwrites P_q(i)), and the Q
+                // tiles alternate, so the tensor core runs P.V_1(i), S_1(i+1) while the softmax warps of
+                // Q tile 0 work on S_0(i+1), and the other way round
+                for (int i = 0; ok && i < n; i++) {
+                    ok = wait_v(i);
+                    for (int q = 0; q < nqt && ok; q++) {
+                        ok = mma_pv(i, q);
+                        if (ok && i + 1 < n) {
+                            if (q == 0) ok = wait_k(i + 1);
+                            if (ok) mma_s(i + 1, q);
                         }
                     }
-                    umma_commit(&o_done[2 * q + (i & 1)]);
+                    if (!ok) break;
+                    release_v(i);
+                    if (i + 1 < n) release_k(i + 1);
                 }
-                if (!ok) break;
-                for (int p = 0; p < NP; p++) umma_commit(&empty_v[(i * NP + p) % C::NEV]);
             }
         }
     }
@@ -623,31 +710,31 @@ fa_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant
 }
 
 // kernel attributes, once per device
-template <int HD, int NQT, int NP, int PL>
+template <int HD, int NQT, int NP, int PL, int BN>
 cudaError_t prepare_t() {
     static std::once_flag once[kMaxDevices];
     static cudaError_t status[kMaxDevices];
     return once_per_device(once, status, [] {
-        using C = PreCfg<HD, NQT, NP>;
-        cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL>,
+        using C = PreCfg<HD, NQT, NP, BN>;
+        cudaError_t e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL, BN>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM + 1024);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL>, cudaFuncAttributeNonPortableClusterSizeAllowed,
-                                     1);
+            e = cudaFuncSetAttribute(fa_prefill_kernel<HD, NQT, NP, PL, BN>,
+                                     cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         return e;
     });
 }
 
 // Splits of the key range per CTA (one CTA per SM, no clusters): minimise (waves) x (per-CTA
-// tiles + a merge cost of ~6 tiles when split), at most 8 splits and at least 2 tiles each,
-// within the workspace (partials) and ticket capacity.
-int pick_splits(int units, int tiles, size_t per_split_floats, size_t ws_floats, int n_tickets) {
+// tiles + a merge cost of ~merge_tiles tiles when split; ~6 tiles of 64 keys), at most 8 splits and
+// at least 2 tiles each, within the workspace (partials) and ticket capacity.
+int pick_splits(int units, int tiles, size_t per_split_floats, size_t ws_floats, int n_tickets, double merge_tiles) {
     int best = 1;
     double best_t = 1e30;
     for (int s = 1; s <= 8; s++) {
         if (s > 1 && (tiles / s < 2 || (size_t)units * s * per_split_floats > ws_floats || 2 * units > n_tickets)) break;
         const double waves = std::ceil((double)units * s / kNumSMs);
-        const double t = waves * ((double)tiles / s + (s > 1 ? 6.0 : 0.0));
+        const double t = waves * ((double)tiles / s + (s > 1 ? merge_tiles : 0.0));
         if (t < best_t - 1e-9) {
             best_t = t;
             best = s;
@@ -656,11 +743,11 @@ int pick_splits(int units, int tiles, size_t per_split_floats, size_t ws_floats,
     return best;
 }
 
-template <int HD, int NQT, int NP, int PL = NP>
+template <int HD, int NQT, int NP, int PL = NP, int BN = 64>
 cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensorMap* tv, const CUtensorMap* tk2,
                      const CUtensorMap* tv2, float* ws, size_t ws_floats, int* tickets, int n_tickets, cudaStream_t st) {
-    using C = PreCfg<HD, NQT, NP>;
-    cudaError_t e = prepare_t<HD, NQT, NP, PL>();
+    using C = PreCfg<HD, NQT, NP, BN>;
+    cudaError_t e = prepare_t<HD, NQT, NP, PL, BN>();
     if (e != cudaSuccess) return e;
     AttnArgs a = a_in;
     const int QPT = 128 / a.G;
@@ -669,7 +756,9 @@ cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensor
     // key tiles of a typical CTA (host value of the causal base; a device-side base uses max keys)
     const int keys = a.causal_base_dev ? a.S : std::min(a.S, a.causal_base + std::min(NQT * QPT, a.T));
     const size_t per_split = (size_t)C::ROWS * (HD + 2);
-    a.n_splits = (ws && tickets) ? pick_splits(units, (keys + C::BN - 1) / C::BN, per_split, ws_floats, n_tickets) : 1;
+    a.n_splits = (ws && tickets) ? pick_splits(units, (keys + C::BN - 1) / C::BN, per_split, ws_floats, n_tickets,
+                                               6.0 * 64 / C::BN)
+                                 : 1;
     a.cluster_merge = 0;
     if (a.n_splits > 1) {
         a.ws_o = ws;
@@ -688,7 +777,7 @@ cudaError_t launch_t(const AttnArgs& a_in, const CUtensorMap* tk, const CUtensor
                                  CU_TENSOR_MAP_SWIZZLE_128B) ? 1 : 0;
     }
     dim3 grid((unsigned)a.n_splits, (unsigned)n_cta_q, (unsigned)a.NKV);
-    return launch_pdl(fa_prefill_kernel<HD, NQT, NP, PL>, grid, dim3(C::THREADS), (size_t)(C::SMEM + 1024), st, *tk, *tv,
+    return launch_pdl(fa_prefill_kernel<HD, NQT, NP, PL, BN>, grid, dim3(C::THREADS), (size_t)(C::SMEM + 1024), st, *tk, *tv,
                       NP == 2 ? *tk2 : *tk, NP == 2 ? *tv2 : *tv, tq, a);
 }
 
@@ -753,9 +842,11 @@ cudaError_t launch_prefill(const AttnArgs& a, int head_dim, const CUtensorMap* t
     const bool parts = tk_lo && tv_lo;
     // two query tiles per CTA when the chunk has them (each K/V tile then feeds 256 query rows)
     if (head_dim == 128) {
+        // two query tiles of an f16 cache: 128-key tiles, the Q tiles alternating on the tensor core
         if (a.T * a.G > 128)
             return parts ? launch_t<128, 2, 2>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st)
-                         : launch_t<128, 2, 1, kF16PParts>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st);
+                         : launch_t<128, 2, 1, kF16PParts, 128>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets,
+                                                                 n_tickets, st);
         return parts ? launch_t<128, 1, 2>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st)
                      : launch_t<128, 1, 1, kF16PParts>(a, tk, tv, tk_lo, tv_lo, ws, ws_floats, tickets, n_tickets, st);
     }

@@ -83,6 +83,7 @@ struct AttnArgs {
     float* ws_o;            // split partials [tile][split][16][HD]
     float* ws_ml;           // [tile][split][16][2]
     int* tickets;           // [tile], zero between launches
+    int merge_levels;       // GQA ticket merge: 2 = groups of 16 splits first (tickets[NKV + kvh*groups + g] too)
     int* err;
     // fused append (f16 cache, decode kernel): rows [cbase, cbase + n_new) come from knew/vnew
     // (row stride new_nb_t bytes) and are written to kc_w/vc_w while being attended

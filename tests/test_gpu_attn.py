@@ -131,6 +131,12 @@ def test_short_chunks(orc, T, n_past):
     (256, 4, 16, 512, 1024),     # config 4 geometry (f16 cache), a 512-token chunk
     (128, 2, 2, 200, 37),        # GQA 1:1 -> 128 queries per tile, ragged last tile
     (128, 8, 64, 70, 500),       # GQA 8:1 -> 16 queries per tile
+    # two query tiles per CTA over 128-key tiles: one key tile, ragged key ends, long causal chunks,
+    # and a last CTA with a single live query tile
+    (128, 8, 32, 64, 0),
+    (128, 8, 32, 300, 1000),
+    (128, 8, 32, 1000, 0),
+    (128, 4, 16, 520, 333),
 ])
 def test_prefill_chunks(orc, hd, nkv, nh, T, n_past):
     """Chunked prefill (query rows > 16 per kv head) on the tcgen05 kernel."""
