@@ -772,10 +772,13 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
         const size_t tbase = (size_t)kvh * ns * 16;
         // n_g (row, 4-column) groups over the 256 consumer threads: P threads per group, each merging
         // every P-th of `cnt` partials (slot of partial u: split first + u * stride) online (running
-        // max, rescaled sum) with the (m, l) pairs and partial rows of 8 partials loaded together, so
+        // max, rescaled sum) with the (m, l) pairs and partial rows of kMB partials loaded together, so
         // the merge is a few L2 round trips; then the P partial merges meet in shared memory.  Threads
         // gi < n_g return the merged (M, L, unnormalised O) of their group.
         const int P = max(1, kCThreads / n_g);
+        // partials per batch of loads: 8 within the 96 registers of the two-CTAs-per-SM kernels
+        // (16 spilled), 16 for the one-CTA-per-SM q8_0 kernel
+        constexpr int kMB = C::MIN_BLOCKS == 1 ? 16 : 8;
         float4* part_o = reinterpret_cast<float4*>(smem);                   // [P][n_g]
         float2* part_ml = reinterpret_cast<float2*>(smem + (size_t)P * n_g * sizeof(float4));
         auto merge_partials = [&](int first, int stride, int cnt, float& Mo, float& Lo, float4& Ao) {
@@ -784,11 +787,11 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 const int r = gi / G4, c = (gi % G4) * 4;
                 float M = -INFINITY, L = 0.0f;
                 float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int u0 = sub; u0 < cnt; u0 += 8 * P) {
-                    float2 ml[8];
-                    float4 v[8];
+                for (int u0 = sub; u0 < cnt; u0 += kMB * P) {
+                    float2 ml[kMB];
+                    float4 v[kMB];
 #pragma unroll
-                    for (int uu = 0; uu < 8; uu++) {
+                    for (int uu = 0; uu < kMB; uu++) {
                         const int u = u0 + uu * P;
                         if (u < cnt) {
                             const size_t slot = tbase + (size_t)(first + u * stride) * 16 + r;
@@ -800,13 +803,13 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                     }
                     float mb = M;
 #pragma unroll
-                    for (int uu = 0; uu < 8; uu++) mb = fmaxf(mb, ml[uu].x);
+                    for (int uu = 0; uu < kMB; uu++) mb = fmaxf(mb, ml[uu].x);
                     if (mb == -INFINITY) continue;
                     const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
                     L *= sc;
                     acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
 #pragma unroll
-                    for (int uu = 0; uu < 8; uu++) {
+                    for (int uu = 0; uu < kMB; uu++) {
                         if (ml[uu].x != -INFINITY) {
                             const float w = fast_exp2(ml[uu].x - mb);
                             L += ml[uu].y * w;

@@ -425,10 +425,11 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
         a.ws_o = ws;
         a.ws_ml = ws + n_part * head_dim;
         a.tickets = tickets;
-        // the GQA kernel merges more than 16 splits in two levels when the tickets have room for the
-        // groups' counters
+        // the GQA kernel merges more than 48 splits in two levels (groups of 16 first) when the tickets
+        // have room for the groups' counters; up to 48 one CTA merges them all (config 4's 33 splits:
+        // the extra ticket round trips of two levels measured slower)
         const int groups = ceil_div(a.n_splits, 16);
-        a.merge_levels = (gqa && groups > 1 && (size_t)a.NKV * (1 + groups) <= (size_t)n_tickets) ? 2 : 1;
+        a.merge_levels = (gqa && groups > 3 && (size_t)a.NKV * (1 + groups) <= (size_t)n_tickets) ? 2 : 1;
     }
     if (gqa && a.n_qtiles == 1) return cuda_status(launch_decode_gqa(a, head_dim, kv_type, tk, tv, st));
     return cuda_status(launch_decode(a, head_dim, kv_type, tk, tv, st));
