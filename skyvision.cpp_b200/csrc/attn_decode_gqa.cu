@@ -639,23 +639,23 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                 const uint8_t* vk1 = vk0 + C::HEADB;
                 const uint8_t* vk8 = vk0 + 8 * C::HEADB;
                 const uint8_t* vk9 = vk8 + C::HEADB;
-                const float2 pA = __half22float2(*reinterpret_cast<const __half2*>(&pb0));
-                const float2 pB = __half22float2(*reinterpret_cast<const __half2*>(&pb1));
+                const __half2 pA = *reinterpret_cast<const __half2*>(&pb0);   // keys 2tq, 2tq + 1
+                const __half2 pB = *reinterpret_cast<const __half2*>(&pb1);   // keys 2tq + 8, 2tq + 9
 #pragma unroll
                 for (int blk = 0; blk < HD / kQK8_0; blk++) {
                     const int db = blk * kQ8_0Bytes;
-                    const float x[4] = {pA.x * h2f(*reinterpret_cast<const uint16_t*>(vk0 + db)),
-                                        pA.y * h2f(*reinterpret_cast<const uint16_t*>(vk1 + db)),
-                                        pB.x * h2f(*reinterpret_cast<const uint16_t*>(vk8 + db)),
-                                        pB.y * h2f(*reinterpret_cast<const uint16_t*>(vk9 + db))};
-                    float hi[4], lo[4];
-#pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        hi[k] = __half2float(__float2half_rn(x[k]));
-                        lo[k] = x[k] - hi[k];
-                    }
-                    const uint32_t bh0 = pack_h2(hi[0], hi[1]), bh1 = pack_h2(hi[2], hi[3]);
-                    const uint32_t bl0 = pack_h2(lo[0], lo[1]), bl1 = pack_h2(lo[2], lo[3]);
+                    // P * d in packed f16: hi = HMUL2 rounds the exact product once, lo = HFMA2 rounds
+                    // (P * d - hi) once -- the same two roundings as in f32 then f16, in 2 instructions
+                    const uint32_t dA = __byte_perm(*reinterpret_cast<const uint16_t*>(vk0 + db),
+                                                    *reinterpret_cast<const uint16_t*>(vk1 + db), 0x5410);
+                    const uint32_t dB = __byte_perm(*reinterpret_cast<const uint16_t*>(vk8 + db),
+                                                    *reinterpret_cast<const uint16_t*>(vk9 + db), 0x5410);
+                    const __half2 hA = __hmul2(pA, *reinterpret_cast<const __half2*>(&dA));
+                    const __half2 hB = __hmul2(pB, *reinterpret_cast<const __half2*>(&dB));
+                    const __half2 lA = __hfma2(pA, *reinterpret_cast<const __half2*>(&dA), __hneg2(hA));
+                    const __half2 lB = __hfma2(pB, *reinterpret_cast<const __half2*>(&dB), __hneg2(hB));
+                    const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(&hA), bh1 = *reinterpret_cast<const uint32_t*>(&hB);
+                    const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(&lA), bl1 = *reinterpret_cast<const uint32_t*>(&lB);
 #pragma unroll
                     for (int n = 2 * blk; n < 2 * blk + 2; n++) {
                         const int off = db + 2 + (n & 1) * 16 + 2 * gq;      // dims 16n + 2gq, + 1
