@@ -363,6 +363,9 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
                          "l"(a.wait_ctr), "l"(a.epoch_dev), "r"(a.wait_per_epoch));
     }
     pdl_wait();
+    // n_past first: its load is in flight while the query rows are staged below (it bounds the key
+    // range; read after the query rows it added a second dependent memory round trip per layer)
+    const int cbase = a.causal_base_dev ? __ldg(a.causal_base_dev) : a.causal_base;
 
     // with the gather fused in, the query rows may depend on the previous layer's gathered output:
     // thread 0 waits (bounded) for its arrival count, then the consumer warps go on
@@ -421,7 +424,6 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
     }
 
     // ---- key range of this split
-    const int cbase = a.causal_base_dev ? __ldg(a.causal_base_dev) : a.causal_base;
     const int khi = a.mask_mode == SV_MASK_CAUSAL ? min(a.S, cbase + nq) : a.S;
     const int ks = ks0;
     const int ke = min(khi, ks + a.chunk);
