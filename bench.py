@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-longctx", action="store_true", help="skip the 131072-token kv-head-sharded leg")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="longctx: how each layer's head outputs reach every rank")
+    ap.add_argument("--shards", type=int, default=None,
+                    help="--workload longctx on one GPU: run rank 0's shard of an N-way kv-head split alone")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx", "kernels", "outproj"],
                     help="cfg2: the headline line; longctx: one 131072-token session sharded by kv head; "
                          "kernels: one small launch set of every kernel (for ncu captures)")
@@ -1039,7 +1041,7 @@ def run_kernels(args):
     print(json.dumps({"workload": "kernels", "us_per_launch": times}), flush=True)
 
 
-def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True):
+def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=None):
     """One 131072-token session (config 5's long-context run) sharded by KV head: rank g keeps kv heads
     [g*8/G, (g+1)*8/G) of all 36 layers and their query heads.  Per layer one kernel appends, attends
     on the local heads and stores its output rows straight into every rank's gathered buffer over
@@ -1049,7 +1051,8 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True):
     decode tokens/s of that session with its KV bandwidth per GPU.  With `check`, after the timed
     steps one more step runs and every rank compares (a) its own heads' rows of the last layer, as
     they landed in its gathered buffer, with the CPU oracle over its cache shard and (b) the whole
-    gathered row block with every rank's own rows (bitwise)."""
+    gathered row block with every rank's own rows (bitwise).  `shards` = G > 1 on one GPU: rank 0's shard
+    of a G-way split alone (its kernel without the exchange), to separate the kernel from the exchange."""
     import importlib
     import torch
     import torch.distributed as dist
@@ -1057,7 +1060,13 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True):
     dev = torch.device(f"cuda:{local}")
     stream = torch.cuda.Stream(device=dev)
     S0 = 131072
-    hs = sh.HeadShardedDecode(NH, NKV, HD, rank, world)
+    G = shards or world
+    emulate = G != world
+    if emulate and world != 1:
+        raise SystemExit("--shards emulates one rank on one GPU")
+    if emulate:
+        gather = "none"
+    hs = sh.HeadShardedDecode(NH, NKV, HD, rank, G)
     nkv_l, nh_l = hs.kv_hi - hs.kv_lo, hs.q_hi - hs.q_lo
     kv = sv.KvCache()
     if not kv.alloc(local, L, nkv_l, HD, S0 + K + W + 64):
@@ -1094,7 +1103,8 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True):
                 for layer in range(L):
                     kv.attn_append_at(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE,
                                       out=out_l[layer], stream=stream)
-                    hs.gather(out_l[layer], out_f[layer])
+                    if not emulate:
+                        hs.gather(out_l[layer], out_f[layer])
             else:
                 for layer in range(L):
                     kv.attn_append_at_peer(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE, peer,
@@ -1111,7 +1121,8 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True):
             with torch.cuda.graph(g, stream=stream):
                 step()
             run = g.replay
-            how = ("one CUDA graph per step (attention kernels + NCCL all-gathers)" if peer is None else
+            how = ("one CUDA graph per step (attention kernels)" if emulate else
+                   "one CUDA graph per step (attention kernels + NCCL all-gathers)" if peer is None else
                    "one CUDA graph per step (attention kernels storing into every rank's gathered buffer)")
         except Exception as ex:         # capture of the collective unavailable: eager steps
             g = None
@@ -1144,9 +1155,13 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True):
             barrier(world)
             if peer is not None:
                 got_all = peer.slot(L - 1, (1, NH, HD)).clone()
+                got = got_all[:, hs.q_lo:hs.q_hi].cpu().numpy()
+            elif emulate:
+                got_all = None
+                got = out_l[L - 1].cpu().numpy()
             else:
                 got_all = out_f[L - 1].clone()
-            got = got_all[:, hs.q_lo:hs.q_hi].cpu().numpy()
+                got = got_all[:, hs.q_lo:hs.q_hi].cpu().numpy()
             # (b) every rank's own rows, gathered by NCCL, against this rank's gathered buffer
             if world > 1:
                 parts = [torch.empty_like(got_all[:, hs.q_lo:hs.q_hi]) for _ in range(world)]
@@ -1177,14 +1192,18 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True):
         return None
     row_b = NKV * HD * 2 * 2
     step_bytes = sum(L * ((S0 + i + 1) * row_b + NH * HD * 6) for i in range(K)) / K
+    if emulate:       # one G-th of the session's bytes, on one GPU
+        step_bytes /= G
     hbm, _, _ = measured_peaks()
     res = {
         "metric": "decode attn tokens/s, one 131072-token session sharded by kv head",
         "value": K / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong",
         "workload": "one session of 131072 cached rows, 36 layers, 32q/8kv HD 128 f16 "
-                    f"({nkv_l} kv heads per GPU)", "step": how,
+                    f"({nkv_l} kv heads per GPU)" + (f"; rank 0's shard of a {G}-way split alone, no exchange"
+                                                     if emulate else ""), "step": how,
         "parallelism": f"kv-head sharding over {world} GPU(s), " + (
+            "one rank's kernel, no exchange" if emulate else
             "NCCL all-gather of head outputs per layer" if gather == "nccl" else
             "head outputs stored into every rank's buffer by the attention kernel (NVLink peer memory)"),
         "kv_gbs": step_bytes / (ms_max / K * 1e-3) / 1e9,
@@ -1206,7 +1225,7 @@ def run_longctx(args, world, rank, local):
     """`--workload longctx`: the long-session leg as its own JSON line."""
     from __graft_entry__ import load_package
     sv = load_package()
-    res = longctx_leg(sv, world, rank, local, args.steps, args.warmup, gather=args.gather)
+    res = longctx_leg(sv, world, rank, local, args.steps, args.warmup, gather=args.gather, shards=args.shards)
     if res is None:
         return
     line = {k: res[k] for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
