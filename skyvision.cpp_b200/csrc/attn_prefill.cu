@@ -76,11 +76,9 @@ namespace {
 // (A lazy rescale that lets the running max trail by up to 2^8 saves the O round trips but rounds the
 // dominant weights: with x8 outlier V rows it cost ~1e-3 of max-abs error, measured on the GPU.)
 constexpr float kRescaleLog2 = 0.0f;
-// softmax exponentials per four that run on the FMA pipe (exp2_fma); the rest use the SFU
-#ifndef SVKV_EXP_FMA
-#define SVKV_EXP_FMA 1
-#endif
-constexpr int kExpFma = SVKV_EXP_FMA;
+// softmax exponentials per four that run on the FMA pipe (exp2_fma); the rest use the SFU (two in four
+// measured slower: 490 -> 450 TFLOP/s on the config 2 tail)
+constexpr int kExpFma = 1;
 // P parts on f16 caches (1: P rounded to f16, standard flash-attention precision)
 constexpr int kF16PParts = 1;
 
