@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--no-longctx", action="store_true", help="skip the 131072-token kv-head-sharded leg")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="longctx: how each layer's head outputs reach every rank")
+    ap.add_argument("--exchange", default="words", choices=["words", "counters"],
+                    help="--workload outproj: partials as 64-bit (value, epoch) words, or f32 with band counters")
     ap.add_argument("--shards", type=int, default=None,
                     help="--workload longctx on one GPU: run rank 0's shard of an N-way kv-head split alone")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "longctx", "kernels", "outproj"],
@@ -1302,7 +1304,8 @@ def run_outproj(args, world, rank, local):
     x = torch.randn(L, 1, kl, generator=gen, device=dev).half()
     out = torch.empty(L, 1, D, dtype=torch.float32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
-    peer = sv.Peer(local, rank, world, L, world * D * 4)
+    # slots of 64-bit (value, epoch) words (no counters), or of f32 partials with per-band counters
+    peer = sv.Peer(local, rank, world, L, world * D * (8 if args.exchange == "words" else 4))
     mine = peer.export()
     handles = [None] * world
     if world > 1:
@@ -1353,6 +1356,8 @@ def run_outproj(args, world, rank, local):
         "dtype": "f16", "data": "synthetic",
         "config": {"workload": f"36 layers x (1 x {Ktot // world}) @ ({Ktot // world} x {D}) f16 per rank, partials "
                                "summed over ranks through NVLink peer memory in the same kernel",
+                   "exchange": ("64-bit (value, epoch) words, polled per word" if args.exchange == "words" else
+                                "f32 partials, per-band counters (release add, acquire poll)"),
                    "parallelism": f"head (column) sharding over {world} GPU(s)"},
         "us_per_layer": ms_max / K / L * 1e3,
         "weight_gbs_per_gpu": wbytes / (ms_max / K * 1e-3) / 1e9,

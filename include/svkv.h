@@ -391,10 +391,13 @@ int sv_peer_destroy(sv_peer* p);
  * stride x_nb_t bytes) by its column slice [k_offset, k_offset + K_local) of the f16 projection
  * w (D rows of K_total, 16-byte aligned), and the ranks' partials are summed into out (f32
  * [T][D]) on every rank, in rank order, so every rank gets the same bits.  One kernel: the
- * partials go into every rank's slot `slot` over peer memory and are counted on every rank's
- * counter; each rank waits (bounded, on the device; err_dev, may be NULL, gets
- * SV_DEVERR_TIMEOUT) for the current epoch's partials of all ranks, then sums.  Every rank calls
- * it with the same D, T and slot; slot_bytes >= world * T * D * 4.  Like the attention gather,
+ * partials go into every rank's slot `slot` over peer memory.  With slot_bytes >= world * T * D * 8
+ * each partial travels as one 64-bit word holding the value and the current epoch, and each rank
+ * polls the words it needs until they carry this epoch (no counters, no fences); with
+ * world * T * D * 4 <= slot_bytes < world * T * D * 8 the partials are f32 and counted on every
+ * rank's per-band counter.  Either way each rank waits (bounded, on the device; err_dev, may be
+ * NULL, gets SV_DEVERR_TIMEOUT) for the current epoch's partials of all ranks, then sums.  Every
+ * rank calls it with the same D, T and slot, and the same slot_bytes.  Like the attention gather,
  * each slot is used once per epoch (one slot per layer; *epoch_dev counts steps from 1 and the
  * caller advances it after each step), so consecutive calls use different slots.  T <= 8,
  * K_local <= 4096 and multiples of 8, D <= 18944.  w is read before the kernel's dependency on
@@ -402,8 +405,8 @@ int sv_peer_destroy(sv_peer* p);
  * kernel starts.  The grid is at most one CTA per SM of the device and every CTA waits for the same
  * band of every rank, so all CTAs must be resident at once: a process restricted to a share of the
  * SMs (MPS, green contexts) gets SV_DEVERR_TIMEOUT instead of a result.  If one rank's wait for its
- * own weight rows expires, it does not count its band on any rank, so every rank reports
- * SV_DEVERR_TIMEOUT (no rank sums a stale partial); the peer group must then be recreated.
+ * own weight rows expires, it does not count its band (or store its words) on any rank, so every
+ * rank reports SV_DEVERR_TIMEOUT (no rank sums a stale partial); the peer group must then be recreated.
  * No reference counterpart (the
  * reference runs one process per model); replaces an NCCL all-gather of the attention rows
  * followed by the full projection on every rank. */

@@ -211,6 +211,15 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
 }
 
 // system-scope release add and acquire load of a counter another GPU may update or read
+// one aligned 64-bit word, single-copy atomic across GPUs: a reader sees the whole old or new word
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void red_add_release_sys(unsigned int* p, unsigned int v) {
     asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

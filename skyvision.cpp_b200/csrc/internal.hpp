@@ -231,6 +231,7 @@ struct OutProjLaunch {
     const int32_t* epoch_dev;
     float* out;
     int* err;
+    int ll;                            // slots hold one 64-bit (value, epoch) word per partial
 };
 cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st);
 int out_proj_max_t();

@@ -57,6 +57,7 @@ struct OutProjArgs {
     float* out;                  // [T][D] f32
     int* err;
     int rows_per_round;          // weight rows one round stages (<= kOpMaxRows)
+    int ll;                      // slots of 64-bit (value, epoch) words: no counters, no fences
     uint32_t w_off;              // byte offset of the staged weight rows in dynamic shared memory
 };
 
@@ -111,8 +112,10 @@ __global__ void __launch_bounds__(kOpThreads, 1) out_proj_peer_kernel(const __gr
     // launch does before its dependency wait reads only model constants
     pdl_trigger();
     pdl_wait();
-    if (threadIdx.x == 64)   // the epoch (advanced by the kernel that ends each step), read with x
-        s_target = (unsigned int)(*reinterpret_cast<const volatile int*>(a.epoch_dev)) * (unsigned int)a.n_peers;
+    if (threadIdx.x == 64) {   // the epoch (advanced by the kernel that ends each step), read with x
+        const unsigned int ep = (unsigned int)(*reinterpret_cast<const volatile int*>(a.epoch_dev));
+        s_target = a.ll ? ep : ep * (unsigned int)a.n_peers;
+    }
     if (a.x_vec) {   // 8 elements per 16-byte load (K_local is a multiple of 8, so no load spans two rows)
         for (int i = threadIdx.x; i < T * KL / 8; i += blockDim.x) {
             const int e = i * 8, t = e / KL, k = e % KL;
@@ -189,8 +192,16 @@ __global__ void __launch_bounds__(kOpThreads, 1) out_proj_peer_kernel(const __gr
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
                     if (lane == 0) own[d - d0][t] = s;
-                    if (lane < a.n_peers)   // lane p stores the value into rank p's slot, region [rank]
-                        s_out[lane][((size_t)a.rank * T + t) * a.D + d] = s;
+                    // lane p stores the value into rank p's slot, region [rank] (its own rank's term comes
+                    // from shared memory); with 64-bit words the value travels with the step's epoch
+                    if (lane < a.n_peers && lane != a.rank) {
+                        const size_t idx = ((size_t)a.rank * T + t) * a.D + d;
+                        if (a.ll)
+                            st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(s_out[lane]) + idx,
+                                               ((unsigned long long)s_target << 32) | __float_as_uint(s));
+                        else
+                            s_out[lane][idx] = s;
+                    }
                 }
             }
         }
@@ -200,6 +211,41 @@ __global__ void __launch_bounds__(kOpThreads, 1) out_proj_peer_kernel(const __gr
     // GPUs; with one rank nothing outside this GPU reads the slot, and GPU scope is the cheaper
     // release (measured ~0.7 vs ~2.5 us)
     __syncthreads();
+    if (a.ll) {
+        // ---- 64-bit words: every partial of the other ranks is valid once its word carries this
+        // step's epoch (an older word is a previous step's); poll each, bounded, and sum in rank order.
+        // A rank whose weight row never landed stores nothing, so the peers' polls expire and report it.
+        if (!ok_flag) return;
+        const unsigned int ep = s_target;
+        const unsigned long long* slot = reinterpret_cast<const unsigned long long*>(a.my_slot);
+        for (int i = threadIdx.x; i < T * nb; i += blockDim.x) {
+            const int t = i / nb, d = d0 + i % nb;
+            float s = 0.0f;
+            bool ok = true;
+            for (int r = 0; r < a.n_peers; r++) {
+                if (r == a.rank) {
+                    s += own[d - d0][t];
+                    continue;
+                }
+                const unsigned long long* wp = slot + ((size_t)r * T + t) * a.D + d;
+                unsigned long long v = ld_relaxed_sys_u64(wp);
+                if ((unsigned int)(v >> 32) != ep) {
+                    const uint64_t t0 = globaltimer_ns();
+                    while ((unsigned int)((v = ld_relaxed_sys_u64(wp)) >> 32) != ep) {
+                        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                            if (a.err) atomicOr(a.err, ERRBIT_TIMEOUT);
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+                if (!ok) break;
+                s += __uint_as_float((unsigned int)v);
+            }
+            if (ok) a.out[(size_t)t * a.D + d] = s;
+        }
+        return;
+    }
     if (threadIdx.x == 0) {
         if (!ok_flag) {
             // a row never landed (the error bit is set): before the CTA leaves, wait (bounded) for the
@@ -264,6 +310,7 @@ cudaError_t launch_out_proj_peer(const OutProjLaunch& r, cudaStream_t st) {
     a.epoch_dev = r.epoch_dev;
     a.out = r.out;
     a.err = r.err;
+    a.ll = r.ll;
     static std::once_flag once[kMaxDevices];   // the attribute, once per device
     static cudaError_t status[kMaxDevices];
     const cudaError_t attr = once_per_device(once, status, [] {

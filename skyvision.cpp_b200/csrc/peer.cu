@@ -192,6 +192,8 @@ int sv_out_proj_peer(sv_peer* p, const void* x, int x_type, int64_t x_nb_t, cons
     r.epoch_dev = epoch_dev;
     r.out = out;
     r.err = err_dev;
+    // slots with room for one 64-bit word per partial carry (value, epoch) words: no band counters
+    r.ll = (size_t)p->world * T * D * sizeof(unsigned long long) <= p->slot_bytes ? 1 : 0;
     const cudaError_t e = svkv::launch_out_proj_peer(r, static_cast<cudaStream_t>(stream));
     cudaSetDevice(prev);
     return e == cudaSuccess ? SV_OK : SV_ERR_CUDA;

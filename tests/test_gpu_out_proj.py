@@ -4,7 +4,9 @@ float64 matrix product of the whole projection (qwen3vl_model.cpp:664-667, mul_m
 world = 1 runs in-process (the partial goes to the rank's own slot); world = 2 runs two spawned
 processes, one per GPU, when two GPUs are visible: each rank holds half of the heads, and both
 must end with the full product, bitwise equal between the ranks.  Tolerance: relative 1e-5 of
-the row norm (f16 weights and inputs are exact; f32 accumulation).  NVLS is off.
+the row norm (f16 weights and inputs are exact; f32 accumulation).  NVLS is off.  Both exchange
+forms run: slots with room for a 64-bit (value, epoch) word per partial (no counters) and slots of
+f32 partials with per-band counters.
 """
 import os
 import socket
@@ -26,7 +28,7 @@ def _data(T):
     return x, w
 
 
-def _run_rank(rank, world, port, T, result):
+def _run_rank(rank, world, port, T, result, ll=True):
     import torch.distributed as dist
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     sv = load_package()
@@ -37,7 +39,7 @@ def _run_rank(rank, world, port, T, result):
     x, w = _data(T)
     K = NH * HD
     kl = K // world
-    peer = sv.Peer(rank, rank, world, 2, world * 8 * D * 4)
+    peer = sv.Peer(rank, rank, world, 2, world * T * D * (8 if ll else 4))
     mine = peer.export()
     handles = [None] * world
     if world > 1:
@@ -73,16 +75,18 @@ def _run_rank(rank, world, port, T, result):
 
 
 @pytest.mark.parametrize("T", [1, 5])
-def test_out_proj_single_rank(T):
+@pytest.mark.parametrize("ll", [True, False])
+def test_out_proj_single_rank(T, ll):
     res = {}
-    _run_rank(0, 1, 0, T, res)
+    _run_rank(0, 1, 0, T, res, ll)
     err, flags, _ = res[0]
     assert flags == 0
     assert err <= 1e-5
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_out_proj_two_ranks():
+@pytest.mark.parametrize("ll", [True, False])
+def test_out_proj_two_ranks(ll):
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -90,7 +94,7 @@ def test_out_proj_two_ranks():
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     res = mgr.dict()
-    procs = [ctx.Process(target=_run_rank, args=(r, 2, port, 1, res)) for r in range(2)]
+    procs = [ctx.Process(target=_run_rank, args=(r, 2, port, 1, res, ll)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
