@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the config-5 multi-session leg")
     ap.add_argument("--no-longctx", action="store_true", help="skip the 131072-token kv-head-sharded leg")
-    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl", "outproj"],
                     help="longctx: how each layer's head outputs reach every rank")
     ap.add_argument("--exchange", default="words", choices=["words", "counters"],
                     help="--workload outproj: partials as 64-bit (value, epoch) words, or f32 with band counters")
@@ -506,6 +506,9 @@ def run_svkv(args, world, rank, local):
     batched = None if args.no_batched else run_batched(sv, dev, stream, rank, world, K, W)
     # the path with a data-path exchange: one 131072-token session sharded by kv head over the same GPUs
     longctx = None if args.no_longctx else longctx_leg(sv, world, rank, local, K, max(3, W))
+    # the same session with each layer's attention followed by the row-parallel output projection, the
+    # rank sum fused into it (one exchange per layer, no all-gather of the attention rows)
+    longctx_proj = None if args.no_longctx else longctx_leg(sv, world, rank, local, K, max(3, W), gather="outproj")
     extras = {}
     if world == 1 and not args.no_batched:
         for name, fn in (("config1", run_cfg1), ("config3_eviction", run_cfg3), ("config4_q8_0", run_cfg4),
@@ -569,6 +572,8 @@ def run_svkv(args, world, rank, local):
         line["batched"] = batched
     if longctx is not None:
         line["longctx"] = longctx
+    if longctx_proj is not None:
+        line["longctx_proj"] = longctx_proj
     line.update(extras)
     if world == 1 and not args.no_cpu_baseline:
         n_tok = max(K, 64)
@@ -1133,8 +1138,16 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
         out_f = torch.empty(L, 1, NH, HD, dtype=torch.float32, device=dev)
         max_keys = S0 + K + W + 1
         peer = None
-        if gather == "peer":
-            peer = sv.Peer(local, rank, world, L, NH * HD * 4)
+        proj = gather == "outproj"
+        if proj:
+            # the step after each layer's attention, row-parallel: this rank's heads' rows times its column
+            # slice of the output projection (D x NH/G*HD), the partials summed over ranks in the same
+            # kernel through 64-bit (value, epoch) words -- no all-gather of the attention rows
+            Dp = 2560
+            w_l = (torch.randn(L, Dp, nh_l * HD, generator=gen, device=dev) * 0.02).half()
+            hid = torch.empty(L, 1, Dp, dtype=torch.float32, device=dev)
+        if gather in ("peer", "outproj"):
+            peer = sv.Peer(local, rank, world, L, world * Dp * 8 if proj else NH * HD * 4)
             mine = peer.export()
             if world > 1:
                 handles = [None] * world
@@ -1146,7 +1159,14 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
             barrier(world)
 
         def step():
-            if peer is None:
+            if proj:
+                for layer in range(L):
+                    kv.attn_append_at(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE,
+                                      out=out_l[layer], stream=stream)
+                    peer.out_proj(out_l[layer].view(1, nh_l * HD), w_l[layer], 0, layer, epoch, out=hid[layer],
+                                  stream=stream)
+                sv.counter_add(epoch, 1, stream=stream)
+            elif peer is None:
                 for layer in range(L):
                     kv.attn_append_at(layer, ql[layer], kl[layer], vl[layer], npast, max_keys, SCALE,
                                       out=out_l[layer], stream=stream)
@@ -1169,6 +1189,7 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
                 step()
             run = g.replay
             how = ("one CUDA graph per step (attention kernels)" if emulate else
+                   "one CUDA graph per step (attention + row-parallel output projection kernels)" if proj else
                    "one CUDA graph per step (attention kernels + NCCL all-gathers)" if peer is None else
                    "one CUDA graph per step (attention kernels storing into every rank's gathered buffer)")
         except Exception as ex:         # capture of the collective unavailable: eager steps
@@ -1200,7 +1221,21 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
             step()
             stream.synchronize()
             barrier(world)
-            if peer is not None:
+            if proj:
+                got_all = None
+                got = out_l[L - 1].cpu().numpy()
+                # the projection: every rank's float64 partial of the last layer, summed, against hid
+                part = torch.from_numpy(out_l[L - 1].reshape(1, -1).double().cpu().numpy() @
+                                        w_l[L - 1].double().cpu().numpy().T)
+                parts = [None] * world
+                if world > 1:
+                    dist.all_gather_object(parts, part)
+                else:
+                    parts = [part]
+                pref = sum(parts).numpy()
+                chk["proj_rel_err"] = float(np.abs(hid[L - 1].double().cpu().numpy() - pref).max() /
+                                            max(np.abs(pref).max(), 1e-30))
+            elif peer is not None:
                 got_all = peer.slot(L - 1, (1, NH, HD)).clone()
                 got = got_all[:, hs.q_lo:hs.q_hi].cpu().numpy()
             elif emulate:
@@ -1241,9 +1276,12 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
     step_bytes = sum(L * ((S0 + i + 1) * row_b + NH * HD * 6) for i in range(K)) / K
     if emulate:       # one G-th of the session's bytes, on one GPU
         step_bytes /= G
+    if proj:          # every rank reads its slice of the projection weights
+        step_bytes += L * 2560 * NH * HD * 2
     hbm, _, _ = measured_peaks()
     res = {
-        "metric": "decode attn tokens/s, one 131072-token session sharded by kv head",
+        "metric": ("decode attention + output projection tokens/s" if proj else "decode attn tokens/s") +
+                  ", one 131072-token session sharded by kv head",
         "value": K / (ms_max * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "strong",
         "workload": "one session of 131072 cached rows, 36 layers, 32q/8kv HD 128 f16 "
@@ -1251,6 +1289,8 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
                                                      if emulate else ""), "step": how,
         "parallelism": f"kv-head sharding over {world} GPU(s), " + (
             "one rank's kernel, no exchange" if emulate else
+            "row-parallel output projection, rank partials summed in its kernel through NVLink (64-bit "
+            "(value, epoch) words)" if proj else
             "NCCL all-gather of head outputs per layer" if gather == "nccl" else
             "head outputs stored into every rank's buffer by the attention kernel (NVLink peer memory)"),
         "kv_gbs": step_bytes / (ms_max / K * 1e-3) / 1e9,
@@ -1265,6 +1305,7 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
                                  "max-abs <= 2e-3, rel-L2 <= 1e-3); gathered buffer vs every rank's rows, "
                                  "elements that differ (0 = bitwise equal)")
         assert chk["oracle_max_abs"] <= 2e-3 and chk["oracle_rel_l2"] <= 1e-3 and chk["gather_mismatch"] == 0, chk
+        assert chk.get("proj_rel_err", 0.0) <= 1e-5, chk
     return res
 
 
