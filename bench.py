@@ -1245,7 +1245,7 @@ def longctx_leg(sv, world, rank, local, K, W, gather="peer", check=True, shards=
                 got_all = out_f[L - 1].clone()
                 got = got_all[:, hs.q_lo:hs.q_hi].cpu().numpy()
             # (b) every rank's own rows, gathered by NCCL, against this rank's gathered buffer
-            if world > 1:
+            if world > 1 and got_all is not None:
                 parts = [torch.empty_like(got_all[:, hs.q_lo:hs.q_hi]) for _ in range(world)]
                 dist.all_gather(parts, got_all[:, hs.q_lo:hs.q_hi].contiguous())
                 whole = torch.cat(parts, dim=1)
