@@ -51,7 +51,8 @@ constexpr int kMergeGroup = 16;            // partials one CTA merges at most (t
 
 constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-template <int HD, int KVT>
+// DEEP (f16, long splits over few kv heads): a 6-stage ring at one CTA per SM instead of 3 stages at two
+template <int HD, int KVT, bool DEEP = false>
 struct GqaCfg {
     static constexpr bool Q8 = KVT == SV_TYPE_Q8_0;
     static constexpr int COLS = 64;                       // f16 columns per TMA box (128-byte swizzle span)
@@ -62,8 +63,8 @@ struct GqaCfg {
     static constexpr int TILE_B = Q8 ? kBK * HEADB : NB * BOXB;          // K (or V) bytes per tile
     static constexpr int STAGE_B = align_up(2 * TILE_B, 1024);
     // f16 HD 64/128: ~96 KB ring, two CTAs per SM; q8_0 HD 256: one CTA per SM, deeper ring
-    static constexpr int STAGES = Q8 ? 4 : (HD == 128 ? 3 : 6);
-    static constexpr int MIN_BLOCKS = Q8 ? 1 : 2;
+    static constexpr int STAGES = Q8 ? 4 : ((HD == 128 && !DEEP) ? 3 : 6);
+    static constexpr int MIN_BLOCKS = (Q8 || DEEP) ? 1 : 2;
     static constexpr int ROWS_MAX = HD >= 256 ? 4 : kRows;              // query rows per kv head
     static constexpr int RING_B = STAGES * STAGE_B;
     static constexpr int CW_LD = HD + 4;                  // padded row of the warp-combine scratch
@@ -204,11 +205,11 @@ __device__ __forceinline__ void wait_gather(const AttnArgs& a) {
     }
 }
 
-template <int HD, int KVT, bool kPeer>
-__global__ void __launch_bounds__(kThreads, GqaCfg<HD, KVT>::MIN_BLOCKS)
+template <int HD, int KVT, bool kPeer, bool kDeep>
+__global__ void __launch_bounds__(kThreads, GqaCfg<HD, KVT, kDeep>::MIN_BLOCKS)
 fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                      const __grid_constant__ AttnArgs a) {
-    using C = GqaCfg<HD, KVT>;
+    using C = GqaCfg<HD, KVT, kDeep>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
@@ -919,31 +920,33 @@ fa_decode_gqa_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_const
 }
 
 // kernel attributes, once per device
-template <int HD, int KVT, bool kPeer = false>
+template <int HD, int KVT, bool kPeer = false, bool kDeep = false>
 cudaError_t prepare_gqa() {
     static std::once_flag once[kMaxDevices];
     static cudaError_t status[kMaxDevices];
     return once_per_device(once, status, [] {
-        cudaError_t e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, GqaCfg<HD, KVT>::SMEM + 1024);
+        cudaError_t e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer, kDeep>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             GqaCfg<HD, KVT, kDeep>::SMEM + 1024);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer>,
+            e = cudaFuncSetAttribute(fa_decode_gqa_kernel<HD, KVT, kPeer, kDeep>,
                                      cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         return e;
     });
 }
 
-template <int HD, int KVT, bool kPeer>
+template <int HD, int KVT, bool kPeer, bool kDeep = false>
 cudaError_t launch_gqa_t(const AttnArgs& a, const CUtensorMap* tk, const CUtensorMap* tv, cudaStream_t st) {
-    cudaError_t e = prepare_gqa<HD, KVT, kPeer>();
+    cudaError_t e = prepare_gqa<HD, KVT, kPeer, kDeep>();
     if (e != cudaSuccess) return e;
     // a cluster merge adds one merger CTA per kv head (cluster = splits + 1)
     const int nx = a.cluster_merge ? a.n_splits + 1 : a.n_splits;
     dim3 grid((unsigned)nx, (unsigned)a.NKV, 1u);
     // load-balancing cluster placement: measured 6.44 -> 6.29 us per layer on config 2 (36-layer graph;
     // the spread policy measured the same as the default)
-    return launch_pdl_cluster_ex(fa_decode_gqa_kernel<HD, KVT, kPeer>, grid, dim3(kThreads),
-                                 (size_t)GqaCfg<HD, KVT>::SMEM + 1024, st, a.cluster_merge ? nx : 1, true, *tk, *tv, a);
+    return launch_pdl_cluster_ex(fa_decode_gqa_kernel<HD, KVT, kPeer, kDeep>, grid, dim3(kThreads),
+                                 (size_t)GqaCfg<HD, KVT, kDeep>::SMEM + 1024, st, a.cluster_merge ? nx : 1, true, *tk,
+                                 *tv, a);
 }
 
 template <int HD, int KVT>
@@ -960,7 +963,7 @@ int max_cluster_gqa() {
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = GqaCfg<HD, KVT>::SMEM + 1024;
         int n = 0;
-        if (cudaOccupancyMaxPotentialClusterSize(&n, fa_decode_gqa_kernel<HD, KVT, false>, &cfg) != cudaSuccess) {
+        if (cudaOccupancyMaxPotentialClusterSize(&n, fa_decode_gqa_kernel<HD, KVT, false, false>, &cfg) != cudaSuccess) {
             cudaGetLastError();
             n = 1;
         }
@@ -997,8 +1000,12 @@ cudaError_t launch_decode_gqa(const AttnArgs& a, int head_dim, int kv_type, cons
     switch (head_dim) {
         case 64: return peer ? launch_gqa_t<64, SV_TYPE_F16, true>(a, tk, tv, st)
                              : launch_gqa_t<64, SV_TYPE_F16, false>(a, tk, tv, st);
-        case 128: return peer ? launch_gqa_t<128, SV_TYPE_F16, true>(a, tk, tv, st)
-                              : launch_gqa_t<128, SV_TYPE_F16, false>(a, tk, tv, st);
+        case 128:
+            if (a.deep_ring)   // long splits over few kv heads: one CTA per SM, 6-stage ring
+                return peer ? launch_gqa_t<128, SV_TYPE_F16, true, true>(a, tk, tv, st)
+                            : launch_gqa_t<128, SV_TYPE_F16, false, true>(a, tk, tv, st);
+            return peer ? launch_gqa_t<128, SV_TYPE_F16, true>(a, tk, tv, st)
+                        : launch_gqa_t<128, SV_TYPE_F16, false>(a, tk, tv, st);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -84,6 +84,7 @@ struct AttnArgs {
     float* ws_ml;           // [tile][split][16][2]
     int* tickets;           // [tile], zero between launches
     int merge_levels;       // GQA ticket merge: 2 = groups of 16 splits first (tickets[NKV + kvh*groups + g] too)
+    int deep_ring;          // GQA f16 HD 128: one CTA per SM with a 6-stage ring (long splits, few kv heads)
     int* err;
     // fused append (f16 cache, decode kernel): rows [cbase, cbase + n_new) come from knew/vnew
     // (row stride new_nb_t bytes) and are written to kc_w/vc_w while being attended
