@@ -25,8 +25,15 @@
 // cluster does no K/V work; every split pushes its partial into CTA 0's shared
 // memory with st.async (completion counted on CTA 0's mbarrier) and exits, and
 // CTA 0 merges and stores, so no split waits on a cluster-wide barrier.
-// Measured on config 2 (36 layers, S ~ 4.5k): 6.6 us per layer against 8.4 us
+// Measured on config 2 (36 layers, S ~ 4.5k): 6.3 us per layer against 8.4 us
 // for the general split-K kernel.
+//
+// Few kv heads over a long context (a long session's per-GPU shard): the
+// splits outnumber a cluster and publish their partials to the workspace; the
+// last split to take the kv head's ticket merges them, or, beyond 48 splits,
+// the last of each group of 16 merges its group and the last group merger
+// merges the groups.  With more than 48 splits per head (f16, HD 128) the plan
+// runs one CTA per SM with a 6-stage ring (kDeep) instead of two CTAs with 3.
 //
 // Roofline: HBM-bound, 2 * HD * 2 bytes per (key, kv head) + Q and O.
 #include <algorithm>

@@ -25,6 +25,10 @@
 // A slot holds [world][T][D] f32 partials; a slot is rewritten only after every rank has summed it
 // when consecutive layers use different slots (a rank reaches layer l + 2 only after every rank
 // finished layer l).
+// Slots with room for 8 bytes per partial take the words form instead of steps 2-3's counters: each
+// partial goes to the other ranks as one 64-bit store of (value, epoch), single-copy atomic, and the
+// summing CTA polls exactly the words of its band until they carry this step's epoch -- no
+// system-scope release, no counter round trip (2 GPUs: 14.8 -> 7.35 us per layer).
 //
 // Bound: HBM on the weights (D x K_local x 2 bytes per launch) plus two NVLink latencies.
 #include "common.cuh"
