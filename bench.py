@@ -356,13 +356,13 @@ def run_svkv(args, world, rank, local):
         n0 = PRE + TAIL
         max_keys = n0 + max(K, W) + 1
         npast = torch.full((1,), n0, dtype=torch.int32, device=dev)
-        # the step's inputs live in one device buffer (Q, then K, then V) so the end-to-end leg moves
-        # them with one host-to-device copy
-        qn_, kn_ = L * NH * HD, L * ne0
-        dqkv = randn(qn_ + 2 * kn_)
-        dq = dqkv[:qn_].view(L, 1, NH, HD)
-        dk = dqkv[qn_:qn_ + kn_].view(L, 1, ne0)
-        dvv = dqkv[qn_ + kn_:].view(L, 1, ne0)
+        # the step's inputs live in one device buffer, packed per layer (Q_l, K_l, V_l), so the
+        # end-to-end leg moves any run of layers with one host-to-device copy
+        PER = NH * HD + 2 * ne0
+        dqkv = randn(L * PER)
+        dq = dqkv.as_strided((L, 1, NH, HD), (PER, NH * HD, HD, 1))
+        dk = dqkv.as_strided((L, 1, ne0), (PER, ne0, 1), NH * HD)
+        dvv = dqkv.as_strided((L, 1, ne0), (PER, ne0, 1), NH * HD + ne0)
         dout = torch.empty(L, 1, NH, HD, dtype=torch.float32, device=dev)
 
         def step():
@@ -428,30 +428,30 @@ def run_svkv(args, world, rank, local):
 
         # ---- end to end: every step copies that step's Q/K/V (36 layers) from pinned host memory to the
         #      device, runs the 36 layers, copies the attention output back to pinned host memory and waits
-        #      for it on the host.  The copies are captured into the step's CUDA graph in chunks on a
-        #      second stream: layers 2..35's inputs land while layers 0-1 run, and layers 0..31's outputs
-        #      leave while layers 32..35 run, so only the first chunk's inputs and the last chunk's
-        #      outputs are outside the kernel chain (every byte still crosses PCIe in every step).
-        hqkv = torch.empty((qn_ + 2 * kn_,), dtype=torch.float16).pin_memory()       # one step's Q, K, V
+        #      for it on the host.  The copies are captured into the step's CUDA graph, one copy per run of
+        #      layers: layers 0-3's inputs on the compute stream ahead of layer 0, layers 4-35's on a second
+        #      stream while layers 0-3 run (~20 GB/s host to device here: the rest lands before layer 4),
+        #      layers 0-31's outputs on the second stream while layers 32-35 run, layers 32-35's after the
+        #      chain.  Every byte crosses PCIe in every step.  Each cross-stream join in the kernel chain
+        #      costs a few us (the kernel after it starts without its programmatic early launch), so the
+        #      chain has one join for the inputs and none for the outputs.  Measured per step: 259-262 us;
+        #      more, smaller chunks (more joins) 263-269 us; every copy outside the chain 271-281 us; the
+        #      inputs as separate Q, K, V copies of layers 0-1 and 2-35, 267-287 us.
+        hqkv = torch.empty((L * PER,), dtype=torch.float16).pin_memory()       # one step's Q, K, V per layer
         hqkv.copy_(torch.randn(hqkv.shape, generator=torch.Generator().manual_seed(SEED)).half())
         hout = torch.empty((L, 1, NH, HD), dtype=torch.float32).pin_memory()
-        hq = hqkv[:qn_].view(L, 1, NH, HD)
-        hk = hqkv[qn_:qn_ + kn_].view(L, 1, ne0)
-        hv = hqkv[qn_ + kn_:].view(L, 1, ne0)
+        hlay, dlay = hqkv.view(L, PER), dqkv.view(L, PER)
         cs = torch.cuda.Stream(device=dev)
-        L_IN, L_OUT = 2, L - 4          # input chunk [0, L_IN) first; output chunk [0, L_OUT) first
+        L_IN, L_OUT = 4, L - 4          # inputs [0, L_IN) on the compute stream; outputs [0, L_OUT) early
 
         def e2e_step():
-            cs.wait_stream(stream)
-            ev_in0, ev_in1 = torch.cuda.Event(), torch.cuda.Event()
+            ev_in1 = torch.cuda.Event()
             ev_mid, ev_out0 = torch.cuda.Event(), torch.cuda.Event()
+            dlay[:L_IN].copy_(hlay[:L_IN], non_blocking=True)
+            cs.wait_stream(stream)
             with torch.cuda.stream(cs):
-                for lo, hi, ev in ((0, L_IN, ev_in0), (L_IN, L, ev_in1)):
-                    dq[lo:hi].copy_(hq[lo:hi], non_blocking=True)
-                    dk[lo:hi].copy_(hk[lo:hi], non_blocking=True)
-                    dvv[lo:hi].copy_(hv[lo:hi], non_blocking=True)
-                    ev.record(cs)
-            stream.wait_event(ev_in0)
+                dlay[L_IN:].copy_(hlay[L_IN:], non_blocking=True)
+                ev_in1.record(cs)
             for layer in range(L):
                 if layer == L_IN:
                     stream.wait_event(ev_in1)
@@ -558,8 +558,8 @@ def run_svkv(args, world, rank, local):
         },
         "e2e": {"value": world * K / (e2e_ms_max * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "how": "per step, one CUDA graph: pinned H2D of 36 layers' Q/K/V (layers 2-35 overlapping layers "
-                       "0-1), the 36 layers, D2H of the attention output (layers 0-31 overlapping layers 32-35); "
+                "how": "per step, one CUDA graph: pinned H2D of 36 layers' Q/K/V (layers 4-35 overlapping layers "
+                       "0-3), the 36 layers, D2H of the attention output (layers 0-31 overlapping layers 32-35); "
                        "host waits for it"},
         "gpu_launches": launches,
         "clocks": clocks,
