@@ -417,9 +417,8 @@ static int run_attention(sv_kv* kvh, const CUtensorMap* tk, const CUtensorMap* t
         a.cluster_merge = 0;
         // long splits over few kv heads (f16, HD 128; one kv head of a 131072-token session per GPU):
         // one CTA per SM with a 6-stage ring, so more of a split's tiles are in flight (one kv head
-        // 19.3 -> 17.0 us per layer).  The fused peer gather keeps the two-CTAs-per-SM kernel (the
-        // form measured on 2-8 GPUs).
-        if (gqa && kv_type == SV_TYPE_F16 && head_dim == 128 && p.n_splits > 48 && a.n_peers == 0) {
+        // 19.3 -> 17.0 us per layer), with or without the fused peer gather.
+        if (gqa && kv_type == SV_TYPE_F16 && head_dim == 128 && p.n_splits > 48) {
             p = plan_decode(a.T, a.G, a.NKV, span, head_dim, window, ws_floats, tickets ? n_tickets : 0,
                             target_ctas_default());
             a.deep_ring = 1;

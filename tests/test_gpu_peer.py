@@ -5,7 +5,9 @@ world = 1 runs in-process on one GPU (the kernel's stores and counters go to the
 buffer).  world = 2 runs two spawned processes, one per GPU, when two GPUs are visible: each rank
 holds half of the kv heads of one session; the gathered rows of every layer must match the oracle
 of the whole, unsharded session on both ranks.  NVLS is off; the ranks exchange IPC handles over a
-gloo group and exit only between steps.
+gloo group and exit only between steps.  The long cases give each rank few kv heads over thousands of
+keys, so the kernel takes more than 48 key splits per head and runs in its one-CTA-per-SM, 6-stage
+ring form, with the gather fused in the same way.
 """
 import os
 import socket
@@ -17,10 +19,13 @@ import torch
 from __graft_entry__ import load_package
 
 pytestmark = pytest.mark.gpu
-NKV, NH, HD, L, N0, STEPS = 8, 32, 128, 2, 1500, 3
+HD, L, STEPS = 128, 2, 3
+SHORT = (8, 32, 1500)         # kv heads, query heads, cached rows before the first step
+LONG1 = (2, 8, 20000)         # one rank, 2 kv heads: over 48 key splits per head
+LONG2 = (8, 32, 9000)         # two ranks, 4 kv heads each: over 48 key splits per head
 
 
-def _session(orc):
+def _session(orc, NKV, NH, N0):
     """Seeded K/V rows (n0 + steps) per layer, and per step the query and the appended K/V row."""
     ne0 = NKV * HD
     rows = [(orc.normal_f16(61, 10 + l, (N0 + STEPS) * ne0).reshape(N0 + STEPS, ne0),
@@ -29,7 +34,7 @@ def _session(orc):
     return rows, q
 
 
-def _run_rank(rank, world, port, result):
+def _run_rank(rank, world, port, result, shape=SHORT):
     import torch.distributed as dist
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     sv = load_package()
@@ -38,9 +43,10 @@ def _run_rank(rank, world, port, result):
     dev = torch.device(f"cuda:{rank}")
     if world > 1:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    NKV, NH, N0 = shape
     nkv_l, nh_l = NKV // world, NH // world
     kv_lo, q_lo = rank * nkv_l, rank * nh_l
-    rows, q = _session(orc)
+    rows, q = _session(orc, NKV, NH, N0)
     kv = sv.KvCache()
     assert kv.alloc(rank, L, nkv_l, HD, N0 + STEPS + 8)
     td = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.float16)).to(dev)
@@ -89,16 +95,18 @@ def _run_rank(rank, world, port, result):
     result[rank] = (max_err, flags)
 
 
-def test_peer_gather_single_rank():
+@pytest.mark.parametrize("shape", [SHORT, LONG1], ids=["short", "long_few_heads"])
+def test_peer_gather_single_rank(shape):
     res = {}
-    _run_rank(0, 1, 0, res)
+    _run_rank(0, 1, 0, res, shape)
     err, flags = res[0]
     assert flags == 0
     assert err <= 2e-3
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_gather_two_ranks():
+@pytest.mark.parametrize("shape", [SHORT, LONG2], ids=["short", "long"])
+def test_peer_gather_two_ranks(shape):
     import torch.multiprocessing as mp
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -106,7 +114,7 @@ def test_peer_gather_two_ranks():
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     res = mgr.dict()
-    procs = [ctx.Process(target=_run_rank, args=(r, 2, port, res)) for r in range(2)]
+    procs = [ctx.Process(target=_run_rank, args=(r, 2, port, res, shape)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
